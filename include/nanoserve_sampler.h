@@ -1,0 +1,143 @@
+/*
+ * nanoserve_sampler.h -- C ABI of the B200 (sm_100a) token-sampling op.
+ *
+ * This library replaces one Python method of NanoServe:
+ *
+ *   nanoserve/scheduler/sampler.py:21-89   Sampler.sample(logits,
+ *       sampling_params_list, history_token_ids, generators=None)
+ *
+ * The reference runs a chain of ATen ops per row (repetition penalty
+ * sampler.py:31-38, temperature sampler.py:40-51, top-k sampler.py:53-58,
+ * top-p sampler.py:60-73, softmax + NaN guard sampler.py:75-80, greedy
+ * argmax sampler.py:82-83, multinomial sampler.py:84-89).  Here the whole
+ * chain is one kernel launch per call: one HBM pass per vocabulary row,
+ * the row held in the shared memory of an 8-CTA thread-block cluster.
+ *
+ * Everything in this header is plain C: raw pointers, sizes and a stream
+ * handle.  All pointers named "device" must be CUDA device (or managed)
+ * memory of the current device; nothing here allocates device memory.
+ *
+ * Per-row parameters are the reference's DERIVED quantities, so that the
+ * host does the Python-double comparisons exactly as the reference does:
+ *   temperature   = float32(max(t, 1e-6)) if t > 0 else 1.0   (sampler.py:41-46)
+ *   NS_ROW_GREEDY = (t == 0.0)                                  (sampler.py:47-50)
+ *   top_k         = k if 0 < k < vocab else 0 (0 = off)         (sampler.py:55)
+ *   NS_ROW_TOP_P  = (top_p < 1.0); top_p = float32(top_p)       (sampler.py:63)
+ *   NS_ROW_PENALTY= (rp != 1.0 and history non-empty);          (sampler.py:33)
+ *                   repetition_penalty = float32(rp)
+ */
+#ifndef NANOSERVE_SAMPLER_H_
+#define NANOSERVE_SAMPLER_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NS_ABI_VERSION 1
+
+/* status codes returned by every entry point */
+#define NS_OK 0
+#define NS_ERR_INVALID_ARG 1   /* bad pointer / shape / dtype / stride   */
+#define NS_ERR_UNSUPPORTED 2   /* e.g. vocab too large for one cluster   */
+#define NS_ERR_CUDA 3          /* a CUDA runtime call failed             */
+
+/* logits element types */
+#define NS_DTYPE_F32 0
+#define NS_DTYPE_BF16 1
+
+/* output token types */
+#define NS_OUT_I64 0
+#define NS_OUT_I32 1
+
+/* NsRowParams.flags bits */
+#define NS_ROW_GREEDY 0x1u   /* temperature == 0.0: argmax token          */
+#define NS_ROW_TOP_P 0x2u    /* top_p < 1.0: nucleus filter on            */
+#define NS_ROW_PENALTY 0x4u  /* repetition penalty on for this row        */
+#define NS_ROW_SEED 0x8u     /* use NsRowParams.seed as this row's key    */
+
+/* device-side status word bits (NsSampleArgs.status, optional) */
+#define NS_STATUS_BAD_SAMPLE_INDEX 0x1u /* sample_indices[i] out of range */
+#define NS_STATUS_BAD_HISTORY_ID 0x2u   /* history id outside [0, vocab)  */
+#define NS_STATUS_WAIT_TIMEOUT 0x4u     /* a bounded wait gave up         */
+#define NS_STATUS_CAP_OVERFLOW 0x8u     /* candidate list overflowed; the
+                                           row fell back to keeping ties  */
+
+/* One row's sampling parameters (32 bytes, device array [num_rows]).
+ * Mirrors nanoserve/config.py:68-79 SamplingParams (temperature :72,
+ * top_p :73, top_k :74, repetition_penalty :75, seed :79), pre-derived as
+ * described at the top of this file. */
+typedef struct NsRowParams {
+  float temperature;        /* divisor applied to the logits             */
+  float top_p;              /* nucleus mass, used when NS_ROW_TOP_P      */
+  float repetition_penalty; /* used when NS_ROW_PENALTY                  */
+  int32_t top_k;            /* 0 = off                                   */
+  uint32_t flags;           /* NS_ROW_* bits                             */
+  uint32_t reserved;
+  uint64_t seed;            /* per-row Philox key when NS_ROW_SEED       */
+} NsRowParams;
+
+/* Arguments of one sampling step (replaces sampler.py:21-27's signature).
+ *
+ * Row i of the output samples logits row sample_indices[i] (or row i when
+ * sample_indices is NULL).  Histories are CSR: row i's prior token ids are
+ * history_ids[history_offsets[i] .. history_offsets[i+1]).
+ *
+ * Randomness: when uniforms is non-NULL, row i draws with the caller's
+ * uniform uniforms[i] in [0,1); otherwise from Philox4x32-10 with key
+ * (philox_seed, or the row's seed under NS_ROW_SEED) and counter
+ * (philox_offset, row_offset + i).  The draw is an inverse CDF over the
+ * filtered probabilities in vocabulary order.
+ *
+ * Debug outputs (NULL = not written), all [num_rows, vocab] fp32:
+ *   out_penalized : the logits after the repetition penalty, i.e. what the
+ *                   reference leaves in its mutated input (sampler.py:38)
+ *   out_filtered  : scaled logits after top-k/top-p masking, -inf where
+ *                   masked (the tensor softmaxed at sampler.py:76)
+ *   out_probs     : the final probabilities (sampler.py:76-80)
+ * The input logits are never modified. */
+typedef struct NsSampleArgs {
+  const void* logits;          /* device [num_logit_rows, row_stride]      */
+  int32_t logits_dtype;        /* NS_DTYPE_*                               */
+  int32_t vocab_size;          /* V                                        */
+  int64_t num_logit_rows;      /* rows in logits                           */
+  int64_t logits_row_stride;   /* elements between rows (>= V)             */
+  int32_t num_rows;            /* S = rows to sample                       */
+  int32_t out_dtype;           /* NS_OUT_*                                 */
+  const int64_t* sample_indices;     /* device [S] or NULL                 */
+  const NsRowParams* row_params;     /* device [S]                         */
+  const int64_t* history_offsets;    /* device [S+1] or NULL (no history)  */
+  const int32_t* history_ids;        /* device [history_offsets[S]]        */
+  const float* uniforms;             /* device [S] or NULL                 */
+  uint64_t philox_seed;
+  uint64_t philox_offset;
+  int64_t row_offset;                /* global index of row 0 (sharding)   */
+  void* out_tokens;                  /* device [S], int64 or int32         */
+  float* out_penalized;              /* device [S, V] or NULL              */
+  float* out_filtered;               /* device [S, V] or NULL              */
+  float* out_probs;                  /* device [S, V] or NULL              */
+  uint32_t* status;                  /* device [1] or NULL: NS_STATUS_* bits
+                                        OR-ed in by the kernel             */
+} NsSampleArgs;
+
+/* Enqueue one sampling step on `stream` (a cudaStream_t; NULL = legacy
+ * default stream).  Host-side checks only; no host synchronisation, no
+ * allocation.  Replaces sampler.py:21-89 (Sampler.sample). */
+int ns_sample(const NsSampleArgs* args, void* stream);
+
+/* Message for the last non-OK status returned on this host thread. */
+const char* ns_last_error(void);
+
+/* NS_ABI_VERSION of the loaded library. */
+int ns_abi_version(void);
+
+/* Largest vocabulary one cluster can hold for the given dtype. */
+int32_t ns_max_vocab(int32_t logits_dtype);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NANOSERVE_SAMPLER_H_ */

@@ -1,0 +1,217 @@
+// ns_device.cuh -- device helpers for the sm_100a sampling kernel.
+//
+// Inline-PTX wrappers for thread-block-cluster distributed shared memory
+// (mapa / ld / st / red / atom on .shared::cluster), the split cluster
+// barrier, mbarrier-tracked bulk copies (cp.async.bulk, global -> own
+// shared memory, no multicast), plus the scalar arithmetic the sampler
+// needs: correctly rounded division by a per-row constant, an order-
+// preserving float key, and the Philox4x32-10 counter-based generator.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ns {
+
+// ----------------------------------------------------------------- smem / DSMEM
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t dsmem_map(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void dsmem_st_u32(uint32_t a, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void dsmem_st_f32(uint32_t a, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+__device__ __forceinline__ void dsmem_st_u64(uint32_t a, uint64_t v) {
+  asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(a), "l"(v) : "memory");
+}
+__device__ __forceinline__ void dsmem_st_f64(uint32_t a, double v) {
+  asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(a), "d"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_ld_u32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t dsmem_ld_u64(uint32_t a) {
+  uint64_t v;
+  asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ float dsmem_ld_f32(uint32_t a) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ double dsmem_ld_f64(uint32_t a) {
+  double v;
+  asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void dsmem_red_add_u32(uint32_t a, uint32_t v) {
+  asm volatile("red.shared::cluster.add.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_atom_add_u32(uint32_t a, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.shared::cluster.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(a), "r"(v) : "memory");
+  return old;
+}
+
+// Split cluster barrier.  Every thread of every CTA must take part, with
+// warp-uniform control flow (the .aligned forms).
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  cluster_arrive();
+  cluster_wait();
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// ----------------------------------------------------------------- mbarrier + bulk copy
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+// Non-blocking probe of phase `parity`; returns true once it completed.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
+// global memory into this CTA's shared memory; completion is counted on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// ----------------------------------------------------------------- float helpers
+// Order-preserving map float -> uint32 (larger float => larger key; -0 < +0).
+__device__ __forceinline__ uint32_t f2key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(uint32_t k) {
+  uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+// 2^x with the SFU (ex2.approx.ftz.f32: no subnormal results).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// e = exp(s - m) for s <= m; the only exponential used anywhere in the
+// kernel, so every path sees identical values for the same (s, m).
+__device__ __forceinline__ float exp_shifted(float s, float m) {
+  return ex2_approx(__fmul_rn(__fsub_rn(s, m), kLog2e));
+}
+
+// Correctly rounded x / t given r = RN(1/t) (Markstein's division by a
+// constant: q0 = RN(x r), rem = x - q0 t exactly via FMA, q = RN(q0 + rem r)).
+// The remainder is exact only when neither x nor q0 is near the underflow
+// range, so operands with min(|x|,|q0|) < 2^-60 or max(|x|,|q0|) > 2^100
+// (zero, tiny, huge, non-finite) take the IEEE division instruction.  With
+// that guard the result equals x / t bit for bit for every fp32 x; this was
+// checked exhaustively over all 2^32 inputs for ten divisors from 1e-6 to
+// 1e30 (tests/test_division_identity.py re-checks a sample on the CPU).
+__device__ __forceinline__ float div_by_const(float x, float t, float r) {
+  float q0 = __fmul_rn(x, r);
+  float rem = __fmaf_rn(-q0, t, x);
+  float q = __fmaf_rn(rem, r, q0);
+  float ax = fabsf(x), aq = fabsf(q0);
+  if (!(fminf(ax, aq) >= 0x1p-60f && fmaxf(ax, aq) <= 0x1p+100f)) q = __fdiv_rn(x, t);
+  return q;
+}
+
+// Repetition penalty on one logit (HF rule, nanoserve/scheduler/sampler.py:37):
+// negative scores are multiplied by rp, others divided by rp (IEEE fp32).
+__device__ __forceinline__ float penalize(float x, float rp) {
+  return (x < 0.0f) ? __fmul_rn(x, rp) : __fdiv_rn(x, rp);
+}
+
+// Fixed-point mass: value * 2^44 rounded toward zero, from the 24-bit
+// significand of a positive normal float with biased exponent `ex`.
+__device__ __forceinline__ uint64_t m24_to_fixed(uint64_t m24sum, int ex) {
+  int sh = ex - 106;  // value = m24 * 2^(ex-150); fixed = value * 2^44
+  if (sh >= 0) return m24sum << sh;
+  if (sh <= -64) return 0ull;
+  return m24sum >> (-sh);
+}
+__device__ __forceinline__ uint64_t f2fixed(float e) {
+  uint32_t b = __float_as_uint(e);
+  if (b == 0u) return 0ull;
+  uint64_t m = (b & 0x7fffffu) | 0x800000u;
+  return m24_to_fixed(m, (int)(b >> 23));
+}
+constexpr double kFixedToReal = 1.0 / 17592186044416.0;  // 2^-44
+
+// ----------------------------------------------------------------- Philox4x32-10
+// Counter-based generator of Salmon, Moraes, Dror and Shaw, "Parallel random
+// numbers: as easy as 1, 2, 3" (SC'11): 10 rounds of the 4x32 Philox
+// S-box with multipliers 0xD2511F53 / 0xCD9E8D57 and Weyl key increments
+// 0x9E3779B9 / 0xBB67AE85.
+struct U4 {
+  uint32_t x, y, z, w;
+};
+__host__ __device__ __forceinline__ U4 philox4x32_10(U4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int i = 0; i < 10; ++i) {
+    uint64_t p0 = (uint64_t)0xD2511F53u * c.x;
+    uint64_t p1 = (uint64_t)0xCD9E8D57u * c.z;
+    uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0;
+    uint32_t hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
+    c = U4{hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0};
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return c;
+}
+// Uniform double in [0,1) with 53 random bits, for one (key, offset, row).
+__host__ __device__ __forceinline__ double philox_uniform(uint64_t key, uint64_t offset, uint64_t row) {
+  U4 c{(uint32_t)offset, (uint32_t)(offset >> 32), (uint32_t)row, (uint32_t)(row >> 32)};
+  U4 o = philox4x32_10(c, (uint32_t)key, (uint32_t)(key >> 32));
+  uint64_t a = o.x >> 5, b = o.y >> 6;  // 27 + 26 bits
+  return (double)((a << 26) | b) * (1.0 / 9007199254740992.0);
+}
+
+}  // namespace ns

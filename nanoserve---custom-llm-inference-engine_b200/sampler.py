@@ -1,0 +1,181 @@
+"""Drop-in replacement for nanoserve/scheduler/sampler.py (``Sampler``).
+
+``Sampler(device).sample(logits, sampling_params_list, history_token_ids,
+generators=None)`` keeps the reference signature (sampler.py:17-27) and
+returns int64 token ids on ``logits.device``, so ``engine.py:247-250`` and
+``Scheduler.update_with_sampled`` work unchanged.  The work is one launch of
+the sm_100a kernel behind ``torch.ops.nanoserve_b200.sample``.
+
+Differences from the reference, all additive:
+
+* the input ``logits`` is never modified (the reference writes the penalised
+  logits back into it, sampler.py:38; ``return_debug=True`` returns them);
+* keyword-only extensions: ``sample_indices`` (fused row gather from a flat
+  ``[T, V]`` fp32/bf16 tensor), ``uniforms`` (one caller uniform per row),
+  ``seed`` (Philox key), ``out_dtype`` (int64 or int32);
+* randomness comes from per-row Philox4x32-10 streams keyed by
+  ``(seed, step, row)`` instead of the global generator that
+  ``torch.multinomial`` uses (sampler.py:87); ``SamplingParams.seed``, which
+  the reference ignores, gives a row its own key;
+* ``generators`` is accepted and ignored, as in the reference (sampler.py:26).
+
+There is no CPU path: the op raises if the CUDA library is not built or the
+tensors are not on a CUDA device.
+"""
+from __future__ import annotations
+
+from pathlib import Path
+from typing import List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import packing
+
+_PKG_DIR = Path(__file__).resolve().parent
+_OPS_PATH = _PKG_DIR / "_nanoserve_ops.so"
+_ops_loaded = False
+
+
+def load_ops() -> None:
+    """Register torch.ops.nanoserve_b200.* (raises if the library was not built)."""
+    global _ops_loaded
+    if _ops_loaded:
+        return
+    if not _OPS_PATH.exists():
+        raise RuntimeError(
+            f"{_OPS_PATH} is missing: build it with __graft_entry__.build() "
+            "(there is no CPU fallback for the sampling op)"
+        )
+    torch.ops.load_library(str(_OPS_PATH))
+    _ops_loaded = True
+
+
+class _Staging:
+    """A reusable pinned host buffer plus the event of its last H2D copy."""
+
+    def __init__(self) -> None:
+        self.host: Optional[torch.Tensor] = None
+        self.event: Optional[torch.cuda.Event] = None
+
+    def get(self, nbytes: int) -> torch.Tensor:
+        if self.event is not None:
+            self.event.synchronize()
+        if self.host is None or self.host.numel() < nbytes:
+            cap = max(nbytes, 1 << 16)
+            self.host = torch.empty(cap, dtype=torch.uint8, pin_memory=True)
+        return self.host[:nbytes]
+
+
+class Sampler:
+    """B200 sampling op with the reference ``Sampler`` interface."""
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self._step = 0
+        self._staging = _Staging()
+        load_ops()
+
+    # -- the reference entry point (sampler.py:21-27) ---------------------
+    def sample(
+        self,
+        logits: torch.Tensor,
+        sampling_params_list: List,
+        history_token_ids: List[List[int]],
+        generators: Optional[List[Optional[torch.Generator]]] = None,
+        *,
+        sample_indices: Optional[torch.Tensor] = None,
+        uniforms: Optional[torch.Tensor] = None,
+        seed: Optional[int] = None,
+        out_dtype: torch.dtype = torch.int64,
+        return_debug: bool = False,
+    ):
+        if logits.dim() != 2:
+            raise ValueError("logits must be [num_seqs, vocab]")
+        if not logits.is_cuda:
+            raise RuntimeError("Sampler.sample needs CUDA logits (no CPU fallback)")
+        vocab = logits.shape[1]
+        S = len(sampling_params_list)
+        if sample_indices is None and logits.shape[0] != S:
+            raise ValueError(f"logits has {logits.shape[0]} rows but {S} sampling params were given")
+        packed = packing.pack(sampling_params_list, history_token_ids, vocab)
+        row_params, offsets, ids = self._upload(packed, logits.device)
+        return self.sample_packed(
+            logits, row_params, offsets, ids,
+            sample_indices=sample_indices, uniforms=uniforms, seed=seed,
+            out_dtype=out_dtype, return_debug=return_debug,
+        )
+
+    # -- pre-packed device inputs (graph-capturable) ------------------------
+    def sample_packed(
+        self,
+        logits: torch.Tensor,
+        row_params: torch.Tensor,
+        history_offsets: Optional[torch.Tensor],
+        history_ids: Optional[torch.Tensor],
+        *,
+        sample_indices: Optional[torch.Tensor] = None,
+        uniforms: Optional[torch.Tensor] = None,
+        seed: Optional[int] = None,
+        offset: Optional[int] = None,
+        row_offset: int = 0,
+        out: Optional[torch.Tensor] = None,
+        out_dtype: torch.dtype = torch.int64,
+        return_debug: bool = False,
+    ):
+        S = row_params.numel() // packing.ROW_DTYPE.itemsize
+        dev = logits.device
+        if logits.stride(1) != 1:
+            logits = logits.contiguous()
+        if out is None:
+            out = torch.empty(S, dtype=out_dtype, device=dev)
+        if seed is None:
+            seed = torch.initial_seed()
+        if offset is None:
+            offset = self._step
+            self._step += 1
+        dbg = None
+        if return_debug:
+            V = logits.shape[1]
+            dbg = {
+                "penalized": torch.empty(S, V, dtype=torch.float32, device=dev),
+                "filtered": torch.empty(S, V, dtype=torch.float32, device=dev),
+                "probs": torch.empty(S, V, dtype=torch.float32, device=dev),
+                "status": torch.zeros(1, dtype=torch.int32, device=dev),
+            }
+        torch.ops.nanoserve_b200.sample(
+            logits, sample_indices, row_params, history_offsets, history_ids, uniforms,
+            int(seed) & 0x7FFFFFFFFFFFFFFF, int(offset), int(row_offset), out,
+            dbg["penalized"] if dbg else None, dbg["filtered"] if dbg else None,
+            dbg["probs"] if dbg else None, dbg["status"] if dbg else None,
+        )
+        if return_debug:
+            return out, dbg
+        return out
+
+    def _upload(self, packed: packing.Packed, device: torch.device):
+        a, b, c, end = packing.layout(packed)
+        host = self._staging.get(end)
+        packing.to_bytes(packed, host.numpy())
+        dev = host.to(device, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._staging.event = ev
+        row_params = dev[a : a + packed.row_params.nbytes]
+        offsets = dev[b : b + packed.offsets.nbytes].view(torch.int64)
+        ids = dev[c : c + packed.ids.nbytes].view(torch.int32) if packed.ids.size else None
+        if ids is None:
+            offsets = None
+        return row_params, offsets, ids
+
+
+def upload_packed(packed: packing.Packed, device) -> tuple:
+    """Device tensors (row_params uint8, offsets int64 or None, ids int32 or None)."""
+    device = torch.device(device)
+    rp = torch.from_numpy(packed.row_params.view(np.uint8).copy()).to(device)
+    if packed.ids.size:
+        off = torch.from_numpy(packed.offsets.copy()).to(device)
+        ids = torch.from_numpy(packed.ids.copy()).to(device)
+    else:
+        off, ids = None, None
+    return rp, off, ids

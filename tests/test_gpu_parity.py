@@ -1,0 +1,163 @@
+"""GPU parity: the sm_100a kernel (through the C ABI) against the numpy oracle.
+
+Tolerances (see tests/gpu_helpers.py): bit-exact penalised and filtered
+logits, greedy and top-k decisions; |dprob| <= 1e-6; sampled tokens equal the
+oracle's inverse CDF except when the uniform lies within 1e-6 of a CDF step;
+top-p sets equal except when the deciding mass lies within 2e-7 of the
+float32 boundary.
+"""
+import importlib
+
+import numpy as np
+import pytest
+import torch
+
+import cases as C
+import gpu_helpers as H
+
+pytestmark = pytest.mark.gpu
+
+W = importlib.import_module(H.PKG + ".workloads")
+
+
+def _check(rep: H.Report):
+    assert not rep.failures, "\n".join(rep.failures)
+
+
+def _dev():
+    assert torch.cuda.is_available(), "GPU test run without a CUDA device"
+    return torch.device("cuda:0")
+
+
+@pytest.mark.parametrize("config,rows", [(1, None), (2, 64), (4, 32), (5, 32)])
+def test_config_parity(config, rows):
+    dev = _dev()
+    w = W.make(config, rows=rows, seed=10 + config)
+    lg = torch.from_numpy(w.logits).to(dev)
+    gpu = H.run_cabi(lg, w.params, w.histories, w.uniforms, sample_indices=w.sample_indices)
+    assert gpu["status"] == 0
+    rep = H.compare(gpu, w.gathered(), w.params, w.histories, w.uniforms)
+    print(f"config {config}: rows {rep.rows}, top-p band {rep.topp_band_rows}, draw band {rep.draw_band_rows}")
+    _check(rep)
+
+
+def test_config3_bf16_gather():
+    dev = _dev()
+    w = W.make(3, rows=16, seed=33)
+    lg = H.to_bf16_tensor(w.logits, dev)
+    assert torch.equal(lg.float().cpu(), torch.from_numpy(w.logits))  # values are exactly bf16
+    gpu = H.run_cabi(lg, w.params, w.histories, w.uniforms, sample_indices=w.sample_indices)
+    assert gpu["status"] == 0
+    _check(H.compare(gpu, w.gathered(), w.params, w.histories, w.uniforms))
+
+
+def test_full_decode_batch_tokens():
+    """Config 2 at its full 256 rows: tokens only (no debug outputs)."""
+    dev = _dev()
+    w = W.make(2, seed=2)
+    lg = torch.from_numpy(w.logits).to(dev)
+    gpu = H.run_cabi(lg, w.params, w.histories, w.uniforms, debug=False)
+    dbg = H.run_cabi(lg, w.params, w.histories, w.uniforms, debug=True)
+    # debug outputs must not change the drawn tokens
+    assert np.array_equal(gpu["tokens"], dbg["tokens"])
+    _check(H.compare(dbg, w.logits, w.params, w.histories, w.uniforms))
+
+
+def test_edge_cases():
+    dev = _dev()
+    case = C.edge_case()
+    lg = torch.from_numpy(case.logits).to(dev)
+    gpu = H.run_cabi(lg, case.params, case.histories, case.uniforms)
+    _check(H.compare(gpu, case.logits, case.params, case.histories, case.uniforms))
+
+
+@pytest.mark.parametrize("V", [1000, 32000, 151936, 50])
+def test_other_vocab_sizes(V):
+    dev = _dev()
+    w = W.make(2, rows=16, seed=V, vocab=V)
+    lg = torch.from_numpy(w.logits).to(dev)
+    gpu = H.run_cabi(lg, w.params, w.histories, w.uniforms)
+    _check(H.compare(gpu, w.logits, w.params, w.histories, w.uniforms))
+
+
+def test_unaligned_rows_take_the_scalar_path():
+    dev = _dev()
+    w = W.make(2, rows=8, seed=5)
+    V = w.logits.shape[1]
+    big = torch.zeros(8, V + 3, device=dev)
+    big[:, 1:V + 1] = torch.from_numpy(w.logits).to(dev)
+    view = big[:, 1:V + 1]  # row stride V+3, base offset 4 bytes: no bulk copies
+    gpu = H.run_cabi(view, w.params, w.histories, w.uniforms)
+    _check(H.compare(gpu, w.logits, w.params, w.histories, w.uniforms))
+
+
+def test_int32_output_and_determinism():
+    dev = _dev()
+    w = W.make(2, rows=32, seed=6)
+    lg = torch.from_numpy(w.logits).to(dev)
+    a = H.run_cabi(lg, w.params, w.histories, None, debug=False, out_i32=True, seed=99, offset=3)
+    b = H.run_cabi(lg, w.params, w.histories, None, debug=False, seed=99, offset=3)
+    assert np.array_equal(a["tokens"], b["tokens"])
+    c = H.run_cabi(lg, w.params, w.histories, None, debug=False, seed=99, offset=4)
+    greedy = np.array([p.temperature == 0.0 for p in w.params])
+    assert np.array_equal(a["tokens"][greedy], c["tokens"][greedy])
+    assert not np.array_equal(a["tokens"][~greedy], c["tokens"][~greedy])
+
+
+def test_row_offset_makes_shards_match_the_whole_batch():
+    dev = _dev()
+    w = W.make(2, rows=32, seed=8)
+    lg = torch.from_numpy(w.logits).to(dev)
+    whole = H.run_cabi(lg, w.params, w.histories, None, debug=False, seed=5, offset=1)["tokens"]
+    parts = []
+    for lo in (0, 16):
+        parts.append(H.run_cabi(lg[lo:lo + 16], w.params[lo:lo + 16], w.histories[lo:lo + 16], None,
+                                debug=False, seed=5, offset=1, row_offset=lo)["tokens"])
+    assert np.array_equal(whole, np.concatenate(parts))
+
+
+def test_input_not_modified():
+    dev = _dev()
+    w = W.make(1, seed=1)
+    lg = torch.from_numpy(w.logits).to(dev)
+    before = lg.clone()
+    H.run_cabi(lg, w.params, w.histories, w.uniforms, sample_indices=w.sample_indices)
+    assert torch.equal(lg, before)
+
+
+def test_bad_inputs_set_status_without_faulting():
+    dev = _dev()
+    w = W.make(2, rows=4, seed=9)
+    lg = torch.from_numpy(w.logits).to(dev)
+    # sample_indices out of range -> status bit, no out-of-bounds access
+    gpu = H.run_cabi(lg, w.params, w.histories, w.uniforms, sample_indices=np.array([0, 1, 2, 99]),
+                     debug=False)
+    assert gpu["status"] & H.cabi.NS_STATUS_BAD_SAMPLE_INDEX
+    # a history id outside the vocabulary (bypassing the host check) -> status bit
+    pk = H.packing.pack(w.params, w.histories, lg.shape[1])
+    ids = pk.ids.copy()
+    if ids.size:
+        ids[0] = lg.shape[1] + 5
+    import ctypes  # noqa: F401
+
+    rp = torch.from_numpy(pk.row_params.view(np.uint8).copy()).to(dev)
+    off = torch.from_numpy(pk.offsets.copy()).to(dev)
+    idt = torch.from_numpy(ids).to(dev)
+    out = torch.empty(4, dtype=torch.int64, device=dev)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+    a = H.cabi.NsSampleArgs()
+    a.logits, a.logits_dtype, a.vocab_size = lg.data_ptr(), 0, lg.shape[1]
+    a.num_logit_rows, a.logits_row_stride, a.num_rows = 4, lg.stride(0), 4
+    a.row_params, a.history_offsets, a.history_ids = rp.data_ptr(), off.data_ptr(), idt.data_ptr()
+    a.out_tokens, a.status = out.data_ptr(), st.data_ptr()
+    H.cabi.ns_sample(a, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    if ids.size:
+        assert st.item() & H.cabi.NS_STATUS_BAD_HISTORY_ID
+
+
+def test_host_side_errors_are_reported():
+    a = H.cabi.NsSampleArgs()
+    a.num_rows = 3
+    with pytest.raises(H.cabi.NsError, match="required"):
+        H.cabi.ns_sample(a, 0)
