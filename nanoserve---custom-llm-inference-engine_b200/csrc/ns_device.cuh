@@ -169,21 +169,31 @@ __device__ __forceinline__ float penalize(float x, float rp) {
   return (x < 0.0f) ? __fmul_rn(x, rp) : __fdiv_rn(x, rp);
 }
 
-// Fixed-point mass: value * 2^44 rounded toward zero, from the 24-bit
-// significand of a positive normal float with biased exponent `ex`.
-__device__ __forceinline__ uint64_t m24_to_fixed(uint64_t m24sum, int ex) {
-  int sh = ex - 106;  // value = m24 * 2^(ex-150); fixed = value * 2^44
-  if (sh >= 0) return m24sum << sh;
-  if (sh <= -64) return 0ull;
-  return m24sum >> (-sh);
+// Approximate mass of one positive normal float for the top-p locator
+// histogram: the top 16 of its 24 significand bits.  Every element of one
+// histogram bucket shares its binary exponent, so a bucket's sum of these
+// values, scaled by 2^(exponent - 142), under-estimates the bucket's true mass
+// by less than a factor (1 - 2^-15).
+__device__ __forceinline__ uint32_t approx_mass16(uint32_t bits) {
+  return ((bits >> 8) & 0x7fffu) | 0x8000u;
 }
-__device__ __forceinline__ uint64_t f2fixed(float e) {
-  uint32_t b = __float_as_uint(e);
-  if (b == 0u) return 0ull;
-  uint64_t m = (b & 0x7fffffu) | 0x800000u;
-  return m24_to_fixed(m, (int)(b >> 23));
+// Scale a sum of approx_mass16 values of one binade (biased exponent ex) to
+// 2^-44 fixed point (truncating).
+__device__ __forceinline__ uint64_t mass16_to_fixed(uint64_t sum, int ex) {
+  const int sh = ex - 98;  // value = sum * 2^(ex-142); fixed = value * 2^44
+  if (sh >= 0) return sum << sh;
+  if (sh <= -64) return 0ull;
+  return sum >> (-sh);
 }
 constexpr double kFixedToReal = 1.0 / 17592186044416.0;  // 2^-44
+
+// max that propagates NaN (any NaN operand gives NaN), used so that one pass
+// both finds the row maximum and detects NaN logits.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
 
 // ----------------------------------------------------------------- Philox4x32-10
 // Counter-based generator of Salmon, Moraes, Dror and Shaw, "Parallel random

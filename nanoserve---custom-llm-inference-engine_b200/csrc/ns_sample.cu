@@ -10,23 +10,25 @@
 //    working on it as soon as it lands.
 //  * Row statistics, histograms and candidate lists are exchanged through
 //    distributed shared memory (st/ld/red/atom .shared::cluster) between
-//    split cluster barriers.  No global scratch memory is used.
+//    cluster barriers.  No global scratch memory is used.
 //  * Three row paths, chosen per row (uniformly across the cluster):
 //      GREEDY   temperature == 0 and no debug output: first-index argmax
-//               (sampler.py:82-83), one exchange.
-//      TOPK     0 < top_k <= kTopkSmall: a per-thread-maximum histogram gives
-//               a lower bound for the k-th largest logit, every element above
-//               it is sent to the leader CTA, which finishes top-k
+//               (sampler.py:82-83); one exchange.
+//      TOPK     0 < top_k <= kTopkSmall: a histogram of per-thread maxima
+//               bounds the k-th largest logit from below; every element
+//               above the bound goes to the leader CTA, which finishes top-k
 //               (sampler.py:53-58), top-p (sampler.py:60-73), softmax and the
 //               inverse-CDF draw on that short list.
 //      GENERAL  anything else: exp(s - max) is computed once per element and
-//               kept in place; top-p uses a mass histogram keyed on the bits
-//               of exp(s - max) (log-spaced buckets), refined until the
-//               crossing bucket fits a candidate list, which the leader sorts
-//               and scans.  Large top-k runs an exact 3-level radix select
-//               first.  The draw scans per-warp masses in vocabulary order.
-//  * Masses that decide filters are 2^-44 fixed point in 64-bit integers,
-//    so every decision is order-independent and bit-reproducible.
+//               kept in place.  Top-p locates its boundary with a histogram
+//               of approximate masses keyed on the bits of exp(s - max)
+//               (log-spaced buckets, one 32-bit shared atomic per element),
+//               narrows it to a window of buckets that must contain the
+//               boundary, then ships the window's elements to the leader,
+//               which ranks them and decides exactly with the exact mass
+//               above the window.  Large top-k runs an exact 3-level radix
+//               select first.  The draw walks per-warp masses in vocabulary
+//               order.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -45,59 +47,66 @@ namespace ns {
 constexpr int kCluster = 8;
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kBins = 2048;          // fine histogram buckets
-constexpr int kCoarse = 32;          // coarse buckets (kBins / kCoarse fine each)
-constexpr int kFinePerCoarse = kBins / kCoarse;
+constexpr int kBins = 4096;          // top-p locator histogram (u32 approximate masses)
+constexpr int kCoarse = 64;          // coarse buckets of kFine fine buckets
+constexpr int kFine = kBins / kCoarse;
+constexpr int kRadixBins = 2048;     // radix-select level histogram (u32 counts), 2 buffers
+constexpr int kRadixCoarse = 32;
 constexpr int kCap = 512;            // leader candidate list capacity
 constexpr int kTopkSmall = 128;      // largest top_k served by the TOPK path
 constexpr int kTmBins = 4096;        // per-thread-maximum histogram (u16 counts)
 constexpr int kMaxSlice = 24576;     // largest slice (elements) one CTA holds
-constexpr uint32_t kOne = 0x3F800000u;  // bits of 1.0f
-constexpr uint64_t kCountOne = 1ull << 40;
-constexpr uint64_t kMassMask = kCountOne - 1ull;
-
-enum : uint32_t { kFlagNonFinite = 1u };
+constexpr int kMaxShift = 17;        // locator buckets cover >= 63.9 binades of exp(s - max)
+constexpr uint32_t kOne = 0x3F800000u;           // bits of 1.0f
+constexpr double kWindowSlack = 1.0 + 0x1p-14;  // > 1 / (1 - 2^-15): locator mass error bound
+constexpr double kFixedScale = 17592186044416.0;  // 2^44
 
 // Fixed-size control block at the start of dynamic shared memory.
 struct __align__(16) Ctl {
   uint64_t mbar[kWarps];
   // per-peer records (slot = peer rank), written by the peers
   float rec_max[kCluster];
-  float rec_minf[kCluster];
-  uint32_t rec_flags[kCluster];
+  float rec_min[kCluster];
+  float rec_amin[kCluster];
   int32_t rec_amax[kCluster];
   int32_t rec_nan[kCluster];
   int32_t rec_pinf[kCluster];
-  double rec_mass[kCluster];
-  // own coarse histogram, double-buffered (peers read it)
-  uint64_t cmass[2][kCoarse];
-  uint32_t ccnt[2][kCoarse];
-  // leader candidate counter (peers add to it)
+  double rec_z[kCluster];
+  double rec_above[kCluster];
+  // own coarse sums, double-buffered (peers read them)
+  double cmass[2][kCoarse];
+  uint32_t ccnt[2][kRadixCoarse];
+  double cz[2];
+  // leader candidate list control (peers add to it)
   uint32_t cand_n;
+  uint32_t overflow;
   // leader broadcast
   float bc_thr;
   int32_t bc_thr_idx;
+  int32_t bc_owner;
   float bc_m;
-  uint32_t bc_flag;
+  double bc_tloc;
   double bc_z;
-  // crossing search result (CTA-local broadcast)
-  int32_t sel_b;
+  // CTA-local results
   int32_t sel_found;
+  int32_t sel_lo;
+  int32_t sel_hi;
   uint32_t sel_cnt;
   uint32_t sel_before_cnt;
-  uint64_t sel_before_mass;
-  uint64_t sel_z;
+  float sel_est;
+  double sel_z;
   // reductions
   float red_a[kWarps];
   float red_b[kWarps];
+  float red_c[kWarps];
   int32_t red_i[kWarps];
-  uint32_t red_u[kWarps];
   int32_t red_j[kWarps];
+  uint32_t red_u[kWarps];
   double wmass[kWarps];
-  uint64_t red_q[kWarps];
+  unsigned long long wfix[kWarps];
   int32_t misc_i;
-  uint32_t mem_n;
   int32_t token;
+  uint32_t mem_n;
 };
 
 struct Layout {
@@ -110,7 +119,7 @@ __host__ __device__ inline Layout make_layout(int W) {
   Layout L;
   size_t o = 0;
   L.ctl = o;    o = align16(o + sizeof(Ctl));
-  L.hist = o;   o = align16(o + sizeof(uint64_t) * kBins);
+  L.hist = o;   o = align16(o + sizeof(uint32_t) * kBins);
   L.bitmap = o; o = align16(o + sizeof(uint32_t) * ((W + 31) / 32));
   L.cand_s = o; o = align16(o + sizeof(float) * kCap);
   L.cand_i = o; o = align16(o + sizeof(int32_t) * kCap);
@@ -123,20 +132,10 @@ __host__ __device__ inline Layout make_layout(int W) {
   return L;
 }
 
-// ---------------------------------------------------------------- reductions
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
+// ---------------------------------------------------------------- warp helpers
 __device__ __forceinline__ float warp_min(float v) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-__device__ __forceinline__ uint32_t warp_or(uint32_t v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v |= __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
 __device__ __forceinline__ int warp_imin(int v) {
@@ -149,12 +148,7 @@ __device__ __forceinline__ double warp_dsum(double v) {
   for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
-__device__ __forceinline__ uint64_t warp_u64_sum(uint64_t v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-// (value, index) argmax with first-index tie break; NaN-free inputs.
+// (value, index) argmax with first-index tie break; NaN values are ignored
 __device__ __forceinline__ void warp_argmax(float& v, int& i) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
@@ -162,15 +156,6 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
     int oi = __shfl_xor_sync(0xffffffffu, i, o);
     if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
   }
-}
-// inclusive scan over lanes (lane 0 first)
-__device__ __forceinline__ uint64_t warp_incl_u64(uint64_t v, int lane) {
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    uint64_t t = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v += t;
-  }
-  return v;
 }
 __device__ __forceinline__ uint32_t warp_incl_u32(uint32_t v, int lane) {
 #pragma unroll
@@ -192,15 +177,13 @@ __device__ __forceinline__ double warp_incl_f64(double v, int lane) {
 // The reference keeps sorted rank j of the top-p pass iff j == 0 or
 // float32(cum[j-1]) <= top_p (sampler.py:66-70); the first rank whose
 // inclusive mass passes this test is the last one kept.
-__device__ __forceinline__ bool topp_crossed(uint64_t cum, uint64_t z, float p) {
-  return (float)((double)cum / (double)z) > p;
+__device__ __forceinline__ bool topp_crossed(double cum, double z, float p) {
+  return (float)(cum / z) > p;
 }
 
 // ---------------------------------------------------------------- per-row context
 struct Row {
-  const NsSampleArgs* a;
-  int row, V, W, base, len, nf4, full4;
-  int f_begin, f_end;
+  int row, V, W, base, len, nf4, full4, f_begin, f_end, chunk;
   uint32_t rank;
   const float* src32;
   const __nv_bfloat16* src16;
@@ -208,22 +191,15 @@ struct Row {
   float T, rT;
   bool t_one, greedy, topp, pen;
   int k;
-  float p;
-  float rp;
-  int64_t h0, h1;
+  float p, rp;
 };
-
-__device__ __forceinline__ void set_status(const NsSampleArgs& a, uint32_t bits) {
-  if (a.status) atomicOr(a.status, bits);
-}
 
 __device__ __forceinline__ float load_scalar(const Row& R, int local) {
   if (R.src16) return __bfloat162float(R.src16[R.base + local]);
   return R.src32[R.base + local];
 }
-
-// Logit after the repetition penalty for one element, from global memory
-// (used for candidate re-computation and debug outputs).
+// Logit after the repetition penalty for one element of this CTA's slice,
+// re-read from global memory (candidate recomputation and debug outputs).
 __device__ __forceinline__ float penalized_from_global(const Row& R, const uint32_t* bitmap, int local) {
   float x = load_scalar(R, local);
   if (R.pen && ((bitmap[local >> 5] >> (local & 31)) & 1u)) x = penalize(x, R.rp);
@@ -232,12 +208,20 @@ __device__ __forceinline__ float penalized_from_global(const Row& R, const uint3
 __device__ __forceinline__ float scaled(const Row& R, float x) {
   return R.t_one ? x : div_by_const(x, R.T, R.rT);
 }
+// Markstein's division without the range guard: exact whenever every |x| of
+// the row lies in [2^-40, 2^80] and the temperature is at most 2^20 (then
+// both |x| and |x/T| stay inside the guard of div_by_const).
+__device__ __forceinline__ float scaled_fast(const Row& R, float x) {
+  const float q0 = __fmul_rn(x, R.rT);
+  return __fmaf_rn(__fmaf_rn(-q0, R.T, x), R.rT, q0);
+}
 
 // Load float4 slot f (4 logits) of this CTA's slice with the penalty applied,
 // store it to shared memory when it did not arrive there by bulk copy or was
-// changed, and emit the penalized debug output.  Elements past the slice
-// end read as -inf.
-__device__ __forceinline__ float4 load_slot(const Row& R, float* vals, const uint32_t* bitmap, int f) {
+// changed, and emit the penalized debug output.  Elements past the slice end
+// read as -inf.
+__device__ __forceinline__ float4 load_slot(const Row& R, float* vals, const uint32_t* bitmap, int f,
+                                            float* pen_out) {
   float4 v;
   const int e0 = f * 4;
   bool dirty = false;
@@ -258,7 +242,7 @@ __device__ __forceinline__ float4 load_slot(const Row& R, float* vals, const uin
     dirty = true;
   }
   if (R.pen) {
-    uint32_t nib = (bitmap[f >> 3] >> ((f & 7) << 2)) & 0xFu;
+    const uint32_t nib = (bitmap[f >> 3] >> ((f & 7) << 2)) & 0xFu;
     if (nib) {
       if (nib & 1u) v.x = penalize(v.x, R.rp);
       if (nib & 2u) v.y = penalize(v.y, R.rp);
@@ -268,24 +252,23 @@ __device__ __forceinline__ float4 load_slot(const Row& R, float* vals, const uin
     }
   }
   if (dirty) reinterpret_cast<float4*>(vals)[f] = v;
-  if (R.a->out_penalized) {
-    float* o = R.a->out_penalized + (int64_t)R.row * R.V + R.base + e0;
-    float t[4] = {v.x, v.y, v.z, v.w};
+  if (pen_out) {
+    const float t[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int c = 0; c < 4; ++c)
-      if (e0 + c < R.len) o[c] = t[c];
+      if (e0 + c < R.len) pen_out[e0 + c] = t[c];
   }
   return v;
 }
 
-// Wait for this warp's bulk copy (bounded; on give-up the status word is set
-// and the kernel carries on so that no cluster barrier is left waiting).
-__device__ __forceinline__ void wait_my_copy(const Row& R, Ctl& ctl, int warp) {
+// Bounded wait for this warp's bulk copy.  On give-up the status word is set
+// and the kernel carries on, so that no cluster barrier is left waiting.
+__device__ __forceinline__ void wait_my_copy(const Row& R, Ctl& ctl, int warp, uint32_t* status) {
   if (!R.tma || R.f_begin >= min(R.f_end, R.full4)) return;
   uint32_t spins = 0;
   while (!mbar_try_wait(&ctl.mbar[warp], 0)) {
     if (++spins > (1u << 22)) {
-      set_status(*R.a, NS_STATUS_WAIT_TIMEOUT);
+      if (status) atomicOr(status, NS_STATUS_WAIT_TIMEOUT);
       break;
     }
     if (spins > 64) __nanosleep(128);
@@ -296,25 +279,29 @@ __device__ __forceinline__ void wait_my_copy(const Row& R, Ctl& ctl, int warp) {
 // logits whose scaled value is at least RN(b/T).
 __device__ float lower_preimage(const Row& R, float b) {
   if (R.t_one || !(b > -INFINITY) || !(b < INFINITY)) return b;
-  float target = div_by_const(b, R.T, R.rT);
+  const float target = div_by_const(b, R.T, R.rT);
   float c = b;
   for (int i = 0; i < 64; ++i) {
-    float d = nextafterf(c, -INFINITY);
+    const float d = nextafterf(c, -INFINITY);
     if (div_by_const(d, R.T, R.rT) == target) c = d; else return c;
   }
   return -INFINITY;
 }
 
-// ---------------------------------------------------------------- CTA-level helpers
+__device__ __forceinline__ void write_token(const NsSampleArgs& a, int row, int tok) {
+  if (a.out_dtype == NS_OUT_I32) reinterpret_cast<int32_t*>(a.out_tokens)[row] = tok;
+  else reinterpret_cast<int64_t*>(a.out_tokens)[row] = tok;
+}
+
 // Block-wide exclusive scan of one u32 per thread (thread 0 first).
 __device__ uint32_t block_excl_u32(Ctl& ctl, uint32_t v, uint32_t& total, int tid) {
   const int lane = tid & 31, warp = tid >> 5;
-  uint32_t inc = warp_incl_u32(v, lane);
+  const uint32_t inc = warp_incl_u32(v, lane);
   if (lane == 31) ctl.red_u[warp] = inc;
   __syncthreads();
   uint32_t wpre = 0, tot = 0;
   for (int w = 0; w < kWarps; ++w) {
-    uint32_t x = ctl.red_u[w];
+    const uint32_t x = ctl.red_u[w];
     if (w < warp) wpre += x;
     tot += x;
   }
@@ -323,132 +310,187 @@ __device__ uint32_t block_excl_u32(Ctl& ctl, uint32_t v, uint32_t& total, int ti
   return wpre + inc - v;
 }
 
-// Cluster-wide crossing search over the fine histogram `hist` (packed
-// count<<40 | m24-sum, kBins buckets, bucket 0 = largest values).
-//   count mode: first bucket whose inclusive count reaches `kneed`;
-//   mass mode:  first bucket whose inclusive mass passes topp_crossed().
-// Bucket b's elements share the biased exponent exps(b) (mass mode only).
-// All CTAs compute the same answer from the peers' coarse sums and the fine
-// buckets of the chosen coarse bucket.  Contains one cluster barrier; the
-// caller must not overwrite `hist` or ctl.c*[buf] until after the next
-// cluster barrier.
-struct BucketExp {
-  uint32_t top;  // key of bucket 0's top element
-  int sh;        // log2 bucket width in keys
-  __device__ __forceinline__ int exp_of(int b) const {
-    uint32_t lo = top - (uint32_t)(b + 1) * (1u << sh) + 1u;
-    return (int)(lo >> 23);
-  }
-};
-
-__device__ void cluster_crossing(Ctl& ctl, const uint64_t* hist, int buf, bool mass_mode, uint32_t kneed,
-                                 uint64_t base_mass, uint64_t zmass, float p, BucketExp be, bool mass_last_valid,
-                                 int tid) {
+// ---------------------------------------------------------------- radix crossing (counts)
+// Over the kRadixBins-bucket count histogram `h` (bucket 0 = largest keys):
+// first bucket whose inclusive count over the whole cluster reaches `kneed`.
+// Contains one cluster barrier; `h` and ctl.ccnt[buf] must stay untouched by
+// this CTA until the next cluster barrier.
+__device__ void radix_crossing(Ctl& ctl, const uint32_t* h, int buf, uint32_t kneed, int tid) {
   const int lane = tid & 31, warp = tid >> 5;
-  // 1) own coarse sums: 16 threads per coarse bucket, 4 fine buckets each
   {
-    const int c = tid >> 4;  // 0..31
-    const int f0 = tid * 4;
+    const int c = tid >> 4;  // 32 coarse buckets x 64 fine; 16 threads each
     uint32_t cnt = 0;
-    uint64_t ms = 0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int b = f0 + j;
-      uint64_t h = hist[b];
-      cnt += (uint32_t)(h >> 40);
-      if (mass_mode && (mass_last_valid || b != kBins - 1)) ms += m24_to_fixed(h & kMassMask, be.exp_of(b));
-    }
+    for (int j = 0; j < 4; ++j) cnt += h[tid * 4 + j];
 #pragma unroll
-    for (int o = 8; o; o >>= 1) {
-      cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-      ms += __shfl_xor_sync(0xffffffffu, ms, o);
-    }
-    if ((tid & 15) == 0) {
-      ctl.ccnt[buf][c] = cnt;
-      ctl.cmass[buf][c] = ms;
-    }
+    for (int o = 8; o; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    if ((tid & 15) == 0) ctl.ccnt[buf][c] = cnt;
   }
   cluster_sync();
   if (warp == 0) {
-    // 2) pull every CTA's coarse sums (lane = coarse bucket)
     uint32_t cnt = 0;
-    uint64_t ms = 0;
-    const uint32_t acnt = smem_addr(&ctl.ccnt[buf][lane]);
-    const uint32_t ams = smem_addr(&ctl.cmass[buf][lane]);
+    const uint32_t ac = smem_addr(&ctl.ccnt[buf][lane]);
 #pragma unroll
-    for (int r = 0; r < kCluster; ++r) {
-      cnt += dsmem_ld_u32(dsmem_map(acnt, r));
-      ms += dsmem_ld_u64(dsmem_map(ams, r));
-    }
-    uint32_t icnt = warp_incl_u32(cnt, lane);
-    uint64_t ims = warp_incl_u64(ms, lane);
-    uint64_t z = zmass;
-    if (z == 0ull) z = __shfl_sync(0xffffffffu, ims, 31);
-    bool hit = mass_mode ? (ms > 0 && topp_crossed(base_mass + ims, z, p)) : (icnt >= kneed);
-    uint32_t bal = __ballot_sync(0xffffffffu, hit);
-    int found = bal != 0u;
-    int cb = found ? __ffs(bal) - 1 : 0;
-    uint32_t before_cnt = __shfl_sync(0xffffffffu, icnt - cnt, cb);
-    uint64_t before_ms = __shfl_sync(0xffffffffu, ims - ms, cb);
-    int b_sel = 0;
-    uint32_t b_cnt = 0, b_before_cnt = 0;
-    uint64_t b_before_ms = 0;
+    for (int r = 0; r < kCluster; ++r) cnt += dsmem_ld_u32(dsmem_map(ac, r));
+    const uint32_t ic = warp_incl_u32(cnt, lane);
+    const uint32_t bal = __ballot_sync(0xffffffffu, ic >= kneed);
+    int found = bal != 0u, bsel = 0;
+    uint32_t bcnt = 0, bbefore = 0;
     if (found) {
-      // 3) pull the fine buckets of coarse bucket cb (2 per lane)
-      uint32_t fc[2];
-      uint64_t fm[2];
+      const int cb = __ffs(bal) - 1;
+      uint32_t run = __shfl_sync(0xffffffffu, ic - cnt, cb);
+      found = 0;
+      for (int hh = 0; hh < 2 && !found; ++hh) {
+        const int b = cb * 64 + hh * 32 + lane;
+        const uint32_t ah = smem_addr(&h[b]);
+        uint32_t f = 0;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int b = cb * kFinePerCoarse + h * 32 + lane;
-        const uint32_t ah = smem_addr(&hist[b]);
-        uint32_t c2 = 0;
-        uint64_t m2 = 0;
-#pragma unroll
-        for (int r = 0; r < kCluster; ++r) {
-          uint64_t x = dsmem_ld_u64(dsmem_map(ah, r));
-          c2 += (uint32_t)(x >> 40);
-          m2 += x & kMassMask;
-        }
-        fc[h] = c2;
-        fm[h] = (mass_mode && (mass_last_valid || b != kBins - 1)) ? m24_to_fixed(m2, be.exp_of(b)) : 0ull;
-      }
-      uint32_t run_c = before_cnt;
-      uint64_t run_m = before_ms;
-      bool done = false;
-#pragma unroll
-      for (int h = 0; h < 2 && !done; ++h) {
-        uint32_t ic = warp_incl_u32(fc[h], lane);
-        uint64_t im = warp_incl_u64(fm[h], lane);
-        bool hit2 = mass_mode ? (fm[h] > 0 && topp_crossed(base_mass + run_m + im, z, p)) : (run_c + ic >= kneed);
-        uint32_t bal2 = __ballot_sync(0xffffffffu, hit2);
-        if (bal2) {
-          int l = __ffs(bal2) - 1;
-          b_sel = cb * kFinePerCoarse + h * 32 + l;
-          b_cnt = __shfl_sync(0xffffffffu, fc[h], l);
-          b_before_cnt = run_c + __shfl_sync(0xffffffffu, ic - fc[h], l);
-          b_before_ms = run_m + __shfl_sync(0xffffffffu, im - fm[h], l);
-          done = true;
+        for (int r = 0; r < kCluster; ++r) f += dsmem_ld_u32(dsmem_map(ah, r));
+        const uint32_t inc = warp_incl_u32(f, lane) + run;
+        const uint32_t b2 = __ballot_sync(0xffffffffu, inc >= kneed);
+        if (b2) {
+          const int l = __ffs(b2) - 1;
+          bsel = cb * 64 + hh * 32 + l;
+          bcnt = __shfl_sync(0xffffffffu, f, l);
+          bbefore = __shfl_sync(0xffffffffu, inc - f, l);
+          found = 1;
         } else {
-          run_c += __shfl_sync(0xffffffffu, ic, 31);
-          run_m += __shfl_sync(0xffffffffu, im, 31);
+          run = __shfl_sync(0xffffffffu, inc, 31);
         }
       }
-      if (!done) found = 0;  // only possible through rounding at the coarse level
     }
     if (lane == 0) {
       ctl.sel_found = found;
-      ctl.sel_b = b_sel;
-      ctl.sel_cnt = b_cnt;
-      ctl.sel_before_cnt = b_before_cnt;
-      ctl.sel_before_mass = b_before_ms;
+      ctl.sel_lo = bsel;
+      ctl.sel_cnt = bcnt;
+      ctl.sel_before_cnt = bbefore;
+    }
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------- top-p locator
+// Bucket b of a locator level covers keys (bits of exp(s - max)) in
+// [top - (b+1)*2^sh + 1, top - b*2^sh]; top + 1 is a multiple of 2^sh, so each
+// bucket lies inside one binade and its elements share one exponent.
+struct Level {
+  uint32_t top;
+  int sh;
+  bool last_is_overflow;  // level 0: the last bucket collects everything below
+  __device__ __forceinline__ uint32_t lo_key(int b) const { return top - (uint32_t)(b + 1) * (1u << sh) + 1u; }
+  __device__ __forceinline__ uint32_t hi_key(int b) const { return top - (uint32_t)b * (1u << sh); }
+  __device__ __forceinline__ double mass(uint32_t sum16, int b) const {
+    if (last_is_overflow && b == kBins - 1) return 0.0;
+    const int ex = (int)(lo_key(b) >> 23);
+    return ldexp((double)sum16, ex - 142);
+  }
+};
+
+// Cluster-wide window search.  Every CTA has its approximate-mass histogram
+// in `h` and its exact mass (the total at level 0, the mass above the level's
+// key range otherwise) in ctl.cz[buf].  Finds the bucket window [lo, hi] that
+// must contain the top-p boundary, given that each bucket's approximate mass
+// is within a factor (1 - 2^-15) of its exact mass, and an estimate of the
+// number of elements in it.  One cluster barrier; the caller must leave `h`
+// and ctl.cmass/cz[buf] untouched until the next cluster barrier.
+__device__ void topp_window(Ctl& ctl, const uint32_t* h, int buf, const Level& lv, bool level0, double zin,
+                            float p, int tid) {
+  const int lane = tid & 31, warp = tid >> 5;
+  {
+    // own coarse sums: 8 threads per coarse bucket, 8 fine buckets each
+    const int c = tid >> 3;
+    double m = 0.0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int b = tid * 8 + j;
+      m += lv.mass(h[b], b);
+    }
+#pragma unroll
+    for (int o = 4; o; o >>= 1) m += __shfl_xor_sync(0xffffffffu, m, o);
+    if ((tid & 7) == 0) ctl.cmass[buf][c] = m;
+  }
+  cluster_sync();
+  if (warp == 0) {
+    double zsum = 0.0;
+#pragma unroll
+    for (int r = 0; r < kCluster; ++r) zsum += dsmem_ld_f64(dsmem_map(smem_addr(&ctl.cz[buf]), r));
+    const double z = level0 ? zsum : zin;
+    const double base = level0 ? 0.0 : zsum;
+    double cm[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const uint32_t ad = smem_addr(&ctl.cmass[buf][hh * 32 + lane]);
+      double s = 0.0;
+#pragma unroll
+      for (int r = 0; r < kCluster; ++r) s += dsmem_ld_f64(dsmem_map(ad, r));
+      cm[hh] = s;
+    }
+    // first coarse buckets where the upper (slack) and the lower estimate cross
+    int c_lo = -1, c_hi = -1;
+    double run = base, pre_lo = 0.0;
+    for (int hh = 0; hh < 2; ++hh) {
+      const double inc = warp_incl_f64(cm[hh], lane) + run;
+      const uint32_t bl = __ballot_sync(0xffffffffu, topp_crossed(inc * kWindowSlack, z, p));
+      const uint32_t bh = __ballot_sync(0xffffffffu, topp_crossed(inc, z, p));
+      if (c_lo < 0 && bl) {
+        const int l = __ffs(bl) - 1;
+        c_lo = hh * 32 + l;
+        pre_lo = __shfl_sync(0xffffffffu, inc - cm[hh], l);
+      }
+      if (c_hi < 0 && bh) c_hi = hh * 32 + __ffs(bh) - 1;
+      run = __shfl_sync(0xffffffffu, inc, 31);
+    }
+    int found = (c_lo >= 0);
+    int b_lo = 0, b_hi = 0;
+    float est = 0.f;
+    if (found) {
+      if (c_hi < 0) c_hi = kCoarse - 1;
+      double frun = pre_lo;
+      int fl = -1, fh = -1;
+      double est_d = 0.0;
+      for (int c = c_lo; c <= c_hi && fh < 0; ++c) {
+        for (int hh = 0; hh < 2 && fh < 0; ++hh) {
+          const int b = c * kFine + hh * 32 + lane;
+          const uint32_t ah = smem_addr(&h[b]);
+          uint32_t s16 = 0;
+#pragma unroll
+          for (int r = 0; r < kCluster; ++r) s16 += dsmem_ld_u32(dsmem_map(ah, r));
+          const double m = lv.mass(s16, b);
+          const double inc = warp_incl_f64(m, lane) + frun;
+          const uint32_t bl = __ballot_sync(0xffffffffu, topp_crossed(inc * kWindowSlack, z, p));
+          const uint32_t bh = __ballot_sync(0xffffffffu, topp_crossed(inc, z, p));
+          const int flo = (fl < 0 && bl) ? c * kFine + hh * 32 + (__ffs(bl) - 1) : fl;
+          const int fhi = bh ? c * kFine + hh * 32 + (__ffs(bh) - 1) : -1;
+          // elements in the window ~ mass / smallest value of the bucket
+          const bool inwin = (flo >= 0) && b >= flo && (fhi < 0 || b <= fhi);
+          const double e_bot = (double)__uint_as_float(lv.lo_key(b));
+          est_d += warp_dsum((inwin && m > 0.0 && e_bot > 0.0) ? m / e_bot : 0.0);
+          fl = flo;
+          fh = fhi;
+          frun = __shfl_sync(0xffffffffu, inc, 31);
+        }
+      }
+      if (fl < 0) fl = c_lo * kFine;
+      if (fh < 0) fh = c_hi * kFine + kFine - 1;
+      if (lv.last_is_overflow && fh == kBins - 1) fh = kBins - 2;
+      if (fl > fh) fl = fh;
+      b_lo = fl;
+      b_hi = fh;
+      est = (float)(est_d * 1.001 + 1.0);
+    }
+    if (lane == 0) {
+      ctl.sel_found = found;
+      ctl.sel_lo = b_lo;
+      ctl.sel_hi = b_hi;
+      ctl.sel_est = est;
       ctl.sel_z = z;
     }
   }
   __syncthreads();
 }
 
-// Rank-by-counting sort of the leader's n candidates: perm[rank] = i with
-// order (s descending, index ascending).  n <= kCap.
+// Rank-by-counting of the leader's n candidates: perm[rank] = i with order
+// (s descending, index ascending).  n <= kCap.
 __device__ void leader_sort(int n, const float* cs, const int32_t* ci, int32_t* perm, int tid) {
   for (int i = tid; i < n; i += kThreads) {
     const float si = cs[i];
@@ -463,12 +505,37 @@ __device__ void leader_sort(int n, const float* cs, const int32_t* ci, int32_t* 
   __syncthreads();
 }
 
+// Per-warp sums of lane values and their total over the CTA (fixed order).
+__device__ __forceinline__ double cta_warp_sums(Ctl& ctl, float lane_v, int lane, int warp, int tid) {
+  const double w = warp_dsum((double)lane_v);
+  if (lane == 0) ctl.wmass[warp] = w;
+  __syncthreads();
+  double s = 0.0;
+  for (int i = 0; i < kWarps; ++i) s += ctl.wmass[i];
+  (void)tid;
+  return s;
+}
+
+// Owner of global row r's mass: first CTA whose mass prefix passes target.
+__device__ __forceinline__ void pick_owner(const double* m, double target, int& owner, double& tloc) {
+  double run = 0.0, last_pre = 0.0;
+  int last = -1;
+  owner = -1;
+  for (int r = 0; r < kCluster; ++r) {
+    const double mr = m[r];
+    if (mr > 0.0) { last = r; last_pre = run; }
+    if (owner < 0 && mr > 0.0 && run + mr > target) { owner = r; tloc = target - run; }
+    run += mr;
+  }
+  if (owner < 0) { owner = last; tloc = target - last_pre; }
+}
+
 // ---------------------------------------------------------------- the kernel
 __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs a, int W, int tma_ok, int vec16_ok) {
   extern __shared__ __align__(128) unsigned char smem[];
   const Layout L = make_layout(W);
   Ctl& ctl = *reinterpret_cast<Ctl*>(smem + L.ctl);
-  uint64_t* hist = reinterpret_cast<uint64_t*>(smem + L.hist);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + L.hist);
   uint32_t* bitmap = reinterpret_cast<uint32_t*>(smem + L.bitmap);
   float* cand_s = reinterpret_cast<float*>(smem + L.cand_s);
   int32_t* cand_i = reinterpret_cast<int32_t*>(smem + L.cand_i);
@@ -477,10 +544,10 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
   float* mem_s = reinterpret_cast<float*>(smem + L.mem_s);
   int32_t* mem_i = reinterpret_cast<int32_t*>(smem + L.mem_i);
   float* vals = reinterpret_cast<float*>(smem + L.vals);
+  float4* vals4 = reinterpret_cast<float4*>(vals);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   Row R;
-  R.a = &a;
   R.rank = cluster_ctarank();
   R.row = blockIdx.x / kCluster;
   R.V = a.vocab_size;
@@ -489,12 +556,11 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
   R.len = max(0, min(W, R.V - R.base));
   R.nf4 = (R.len + 3) >> 2;
   R.full4 = R.len >> 2;
-  {
-    const int chunk = (R.nf4 + kWarps - 1) / kWarps;
-    R.f_begin = min(R.nf4, warp * chunk);
-    R.f_end = min(R.nf4, R.f_begin + chunk);
-  }
+  R.chunk = max(1, (R.nf4 + kWarps - 1) / kWarps);
+  R.f_begin = min(R.nf4, warp * R.chunk);
+  R.f_end = min(R.nf4, R.f_begin + R.chunk);
   const bool leader = (R.rank == 0);
+  uint32_t* const status = a.status;
 
   // source row (fused gather of sample_indices)
   int64_t src = R.row;
@@ -525,26 +591,28 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
   R.p = P.top_p;
   R.k = (P.top_k > 0 && P.top_k < R.V) ? P.top_k : 0;
   R.rp = P.repetition_penalty;
-  R.h0 = R.h1 = 0;
+  int64_t h0 = 0, h1 = 0;
   if (a.history_offsets && (P.flags & NS_ROW_PENALTY)) {
-    R.h0 = a.history_offsets[R.row];
-    R.h1 = a.history_offsets[R.row + 1];
+    h0 = a.history_offsets[R.row];
+    h1 = a.history_offsets[R.row + 1];
   }
-  R.pen = (P.flags & NS_ROW_PENALTY) != 0u && R.h1 > R.h0;
+  R.pen = (P.flags & NS_ROW_PENALTY) != 0u && h1 > h0;
   const bool debug = (a.out_filtered != nullptr) || (a.out_probs != nullptr);
+  const int64_t out_off = (int64_t)R.row * R.V + R.base;
+  float* pen_out = a.out_penalized ? a.out_penalized + out_off : nullptr;
 
   enum { kGreedy, kTopk, kGeneral };
-  int mode = (R.greedy && !debug) ? kGreedy : (R.k > 0 && R.k <= kTopkSmall) ? kTopk : kGeneral;
+  const int mode0 = (R.greedy && !debug) ? kGreedy : (R.k > 0 && R.k <= kTopkSmall) ? kTopk : kGeneral;
 
   // ---------------- setup: barriers, zeroed histograms, penalty bitmap
   if (tid == 0) {
     for (int w = 0; w < kWarps; ++w) mbar_init(&ctl.mbar[w], 1);
     fence_mbar_init();
     ctl.cand_n = 0u;
+    ctl.overflow = 0u;
     ctl.mem_n = 0u;
-    ctl.bc_flag = 0u;
   }
-  for (int i = tid; i < kBins; i += kThreads) hist[i] = 0ull;
+  for (int i = tid; i < kBins / 4; i += kThreads) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
   if (R.pen)
     for (int i = tid; i < (W + 31) / 32; i += kThreads) bitmap[i] = 0u;
   __syncthreads();
@@ -561,18 +629,18 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
   }
   if (R.pen) {
     uint32_t bad = 0;
-    for (int64_t i = R.h0 + tid; i < R.h1; i += kThreads) {
+    for (int64_t i = h0 + tid; i < h1; i += kThreads) {
       const int id = a.history_ids[i];
       if (id < 0 || id >= R.V) { bad = 1; continue; }
       const int local = id - R.base;
       if (local >= 0 && local < R.len) atomicOr(&bitmap[local >> 5], 1u << (local & 31));
     }
-    if (bad && R.rank == 0) set_status(a, NS_STATUS_BAD_HISTORY_ID);
+    if (bad && leader && status) atomicOr(status, NS_STATUS_BAD_HISTORY_ID);
     __syncthreads();
   }
-  if (bad_row && leader && tid == 0) set_status(a, NS_STATUS_BAD_SAMPLE_INDEX);
+  if (bad_row && leader && tid == 0 && status) atomicOr(status, NS_STATUS_BAD_SAMPLE_INDEX);
 
-  wait_my_copy(R, ctl, warp);
+  wait_my_copy(R, ctl, warp, status);
 
   // row uniform
   double u;
@@ -585,99 +653,88 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
   if (!(u >= 0.0)) u = 0.0;
   if (u >= 1.0) u = 0x1.fffffffffffffp-1;
 
-  float4* vals4 = reinterpret_cast<float4*>(vals);
-  const int64_t out_row_off = (int64_t)R.row * R.V;
-
   // ---------------- pass 1 (mode-specific statistics)
-  float st_max = -INFINITY, st_minf = INFINITY, nfacc = 0.0f;
+  float st_max = -INFINITY, st_min = INFINITY, st_amin = INFINITY;
   int st_amax = INT_MAX;
-  if (mode == kGreedy || mode == kGeneral) {
+  if (mode0 == kTopk && !R.greedy) {
     for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
-      float4 v = load_slot(R, vals, bitmap, f);
-      float m4 = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
-      nfacc = __fmaf_rn(__fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(v.z, v.w)), 0.0f, nfacc);
+      const float4 v = load_slot(R, vals, bitmap, f, pen_out);
+      st_max = fmax_nan(st_max, fmax_nan(fmax_nan(v.x, v.y), fmax_nan(v.z, v.w)));
+    }
+  } else {
+    const bool want_min = (mode0 == kGeneral);
+    const bool want_amin = want_min && !R.t_one;
+    for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
+      const float4 v = load_slot(R, vals, bitmap, f, pen_out);
+      const float m4 = fmax_nan(fmax_nan(v.x, v.y), fmax_nan(v.z, v.w));
       if (m4 > st_max) {
-        st_max = m4;
         const int c = (v.x == m4) ? 0 : (v.y == m4) ? 1 : (v.z == m4) ? 2 : 3;
         st_amax = R.base + 4 * f + c;
       }
-      if (mode == kGeneral) {
-        float a0 = v.x > -INFINITY ? v.x : INFINITY;
-        float a1 = v.y > -INFINITY ? v.y : INFINITY;
-        float a2 = v.z > -INFINITY ? v.z : INFINITY;
-        float a3 = v.w > -INFINITY ? v.w : INFINITY;
-        st_minf = fminf(st_minf, fminf(fminf(a0, a1), fminf(a2, a3)));
-      }
+      st_max = fmax_nan(st_max, m4);
+      if (want_min) st_min = fminf(st_min, fminf(fminf(v.x, v.y), fminf(v.z, v.w)));
+      if (want_amin)
+        st_amin = fminf(st_amin, fminf(fminf(fabsf(v.x), fabsf(v.y)), fminf(fabsf(v.z), fabsf(v.w))));
     }
-  } else {  // kTopk: per-thread maxima (with the argmax for greedy rows)
-    for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
-      float4 v = load_slot(R, vals, bitmap, f);
-      float m4 = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
-      nfacc = __fmaf_rn(__fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(v.z, v.w)), 0.0f, nfacc);
-      if (m4 > st_max) {
-        st_max = m4;
-        const int c = (v.x == m4) ? 0 : (v.y == m4) ? 1 : (v.z == m4) ? 2 : 3;
-        st_amax = R.base + 4 * f + c;
-      }
-    }
-    // local histogram of thread maxima (u16 counts packed in u32 words)
-    uint32_t* tm_local = reinterpret_cast<uint32_t*>(hist);
-    const uint32_t b = f2key(st_max) >> 20;
-    atomicAdd(&tm_local[b >> 1], 1u << ((b & 1u) << 4));
   }
-  uint32_t my_flags = (nfacc == nfacc) ? 0u : kFlagNonFinite;
-
-  // CTA reduction of (max, argmax, minf, flags)
+  if (mode0 == kTopk) {
+    // local histogram of thread maxima (u16 counts packed in u32 words)
+    const uint32_t b = f2key(st_max) >> 20;
+    atomicAdd(&hist[b >> 1], 1u << ((b & 1u) << 4));
+  }
+  // CTA reduction of (max with NaN propagation, argmax, min, min |x|)
   {
-    float vmax = st_max;
+    const bool lane_nan = (st_max != st_max);
+    const bool warp_nan = __any_sync(0xffffffffu, lane_nan);
+    float vmax = lane_nan ? -INFINITY : st_max;
     int vi = st_amax;
     warp_argmax(vmax, vi);
-    float vminf = warp_min(st_minf);
-    uint32_t fl = warp_or(my_flags);
+    const float vmin = warp_min(st_min);
+    const float vamin = warp_min(st_amin);
     if (lane == 0) {
-      ctl.red_a[warp] = vmax;
+      ctl.red_a[warp] = warp_nan ? __int_as_float(0x7fc00000) : vmax;
       ctl.red_i[warp] = vi;
-      ctl.red_b[warp] = vminf;
-      ctl.red_u[warp] = fl;
+      ctl.red_b[warp] = vmin;
+      ctl.red_c[warp] = vamin;
     }
     __syncthreads();
     if (tid == 0) {
-      float m = -INFINITY, mf = INFINITY;
+      float m = -INFINITY, mn = INFINITY, amn = INFINITY;
       int mi = INT_MAX;
-      uint32_t f = 0;
+      bool nan_any = false;
       for (int w = 0; w < kWarps; ++w) {
-        float x = ctl.red_a[w];
-        int xi = ctl.red_i[w];
-        if (x > m || (x == m && xi < mi)) { m = x; mi = xi; }
-        mf = fminf(mf, ctl.red_b[w]);
-        f |= ctl.red_u[w];
+        const float x = ctl.red_a[w];
+        const int xi = ctl.red_i[w];
+        if (x != x) nan_any = true;
+        else if (x > m || (x == m && xi < mi)) { m = x; mi = xi; }
+        mn = fminf(mn, ctl.red_b[w]);
+        amn = fminf(amn, ctl.red_c[w]);
       }
-      ctl.red_a[0] = m;
+      ctl.red_a[0] = nan_any ? __int_as_float(0x7fc00000) : m;
       ctl.red_i[0] = mi;
-      ctl.red_b[0] = mf;
-      ctl.red_u[0] = f;
+      ctl.red_b[0] = mn;
+      ctl.red_c[0] = amn;
     }
     __syncthreads();
   }
   const float cta_max = ctl.red_a[0];
   const int cta_amax = ctl.red_i[0];
-  const float cta_minf = ctl.red_b[0];
-  const uint32_t cta_flags = ctl.red_u[0];
+  const float cta_min = ctl.red_b[0];
+  const float cta_amin = ctl.red_c[0];
   __syncthreads();
 
   cluster_wait();  // barrier 0 complete: peers may now be written
 
-  // push this CTA's record to every CTA; TOPK also pushes its maxima histogram
   if (tid < kCluster) {
     const uint32_t r = (uint32_t)tid;
     dsmem_st_f32(dsmem_map(smem_addr(&ctl.rec_max[R.rank]), r), cta_max);
-    dsmem_st_f32(dsmem_map(smem_addr(&ctl.rec_minf[R.rank]), r), cta_minf);
-    dsmem_st_u32(dsmem_map(smem_addr(&ctl.rec_flags[R.rank]), r), cta_flags);
+    dsmem_st_f32(dsmem_map(smem_addr(&ctl.rec_min[R.rank]), r), cta_min);
+    dsmem_st_f32(dsmem_map(smem_addr(&ctl.rec_amin[R.rank]), r), cta_amin);
     dsmem_st_u32(dsmem_map(smem_addr(&ctl.rec_amax[R.rank]), r), (uint32_t)cta_amax);
   }
-  if (mode == kTopk) {
-    const uint32_t* tm_local = reinterpret_cast<const uint32_t*>(hist);
-    uint32_t* tm_global = reinterpret_cast<uint32_t*>(hist) + kTmBins / 2;
+  if (mode0 == kTopk) {
+    const uint32_t* tm_local = hist;
+    uint32_t* tm_global = hist + kTmBins / 2;
     for (int w = tid; w < kTmBins / 2; w += kThreads) {
       const uint32_t v = tm_local[w];
       if (v) {
@@ -689,84 +746,76 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
   }
   cluster_sync();  // barrier 1: records (and maxima histograms) delivered
 
-  // ---------------- non-finite rows: classify on a rescan
-  uint32_t any_nf = 0;
-  float gmax = -INFINITY, gminf = INFINITY;
+  float gmax = -INFINITY, gmin = INFINITY, gamin = INFINITY;
   int gamax = INT_MAX;
+  bool gnan = false;
   for (int r = 0; r < kCluster; ++r) {
-    any_nf |= ctl.rec_flags[r];
     const float x = ctl.rec_max[r];
-    if (x > gmax) { gmax = x; gamax = ctl.rec_amax[r]; }
-    gminf = fminf(gminf, ctl.rec_minf[r]);
+    if (x != x) gnan = true;
+    else if (x > gmax) { gmax = x; gamax = ctl.rec_amax[r]; }
+    gmin = fminf(gmin, ctl.rec_min[r]);
+    gamin = fminf(gamin, ctl.rec_amin[r]);
   }
-  if (gmax == -INFINITY) gamax = 0;  // all -inf (or empty): torch.argmax -> 0
+  if (gmax == -INFINITY) gamax = 0;
 
-  if (any_nf) {
-    int my_nan = INT_MAX, my_pinf = INT_MAX;
-    for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
-      const float4 v = vals4[f];
-      const float t[4] = {v.x, v.y, v.z, v.w};
+  // ---------------- rows whose softmax is NaN: uniform 1/V (sampler.py:76-80)
+  if (gnan || gmax == INFINITY || gmax == -INFINITY) {
+    int tok = 0;
+    if (R.greedy) {
+      // torch.argmax: the first NaN, else the first +inf, else index 0
+      int my_nan = INT_MAX, my_pinf = INT_MAX;
+      for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
+        const float4 v = vals4[f];
+        const float t[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int idx = R.base + 4 * f + c;
-        if (4 * f + c < R.len) {
-          if (t[c] != t[c]) my_nan = min(my_nan, idx);
-          if (t[c] == INFINITY) my_pinf = min(my_pinf, idx);
+        for (int c = 0; c < 4; ++c) {
+          if (4 * f + c < R.len) {
+            const int idx = R.base + 4 * f + c;
+            if (t[c] != t[c]) my_nan = min(my_nan, idx);
+            if (t[c] == INFINITY) my_pinf = min(my_pinf, idx);
+          }
         }
       }
-    }
-    my_nan = warp_imin(my_nan);
-    my_pinf = warp_imin(my_pinf);
-    if (lane == 0) { ctl.red_i[warp] = my_nan; ctl.red_j[warp] = my_pinf; }
-    __syncthreads();
-    if (tid < kCluster) {
-      int n = INT_MAX, q = INT_MAX;
-      for (int w = 0; w < kWarps; ++w) { n = min(n, ctl.red_i[w]); q = min(q, ctl.red_j[w]); }
-      dsmem_st_u32(dsmem_map(smem_addr(&ctl.rec_nan[R.rank]), tid), (uint32_t)n);
-      dsmem_st_u32(dsmem_map(smem_addr(&ctl.rec_pinf[R.rank]), tid), (uint32_t)q);
-    }
-    cluster_sync();
-    int gnan = INT_MAX, gpinf = INT_MAX;
-    for (int r = 0; r < kCluster; ++r) {
-      gnan = min(gnan, ctl.rec_nan[r]);
-      gpinf = min(gpinf, ctl.rec_pinf[r]);
-    }
-    if (gnan != INT_MAX || gpinf != INT_MAX || gmax == -INFINITY) {
-      // softmax of this row is NaN -> uniform 1/V (sampler.py:76-80)
-      if (leader && tid == 0) {
-        int tok;
-        if (R.greedy) tok = (gnan != INT_MAX) ? gnan : (gpinf != INT_MAX) ? gpinf : 0;
-        else tok = min(R.V - 1, (int)(u * (double)R.V));
-        if (a.out_dtype == NS_OUT_I32) reinterpret_cast<int32_t*>(a.out_tokens)[R.row] = tok;
-        else reinterpret_cast<int64_t*>(a.out_tokens)[R.row] = tok;
+      my_nan = warp_imin(my_nan);
+      my_pinf = warp_imin(my_pinf);
+      if (lane == 0) { ctl.red_i[warp] = my_nan; ctl.red_j[warp] = my_pinf; }
+      __syncthreads();
+      if (tid < kCluster) {
+        int n = INT_MAX, q = INT_MAX;
+        for (int w = 0; w < kWarps; ++w) { n = min(n, ctl.red_i[w]); q = min(q, ctl.red_j[w]); }
+        dsmem_st_u32(dsmem_map(smem_addr(&ctl.rec_nan[R.rank]), tid), (uint32_t)n);
+        dsmem_st_u32(dsmem_map(smem_addr(&ctl.rec_pinf[R.rank]), tid), (uint32_t)q);
       }
-      if (debug) {
-        const float pu = 1.0f / (float)R.V;
-        for (int i = tid; i < R.len; i += kThreads) {
-          if (a.out_probs) a.out_probs[out_row_off + R.base + i] = pu;
-          if (a.out_filtered) a.out_filtered[out_row_off + R.base + i] = scaled(R, vals[i]);
-        }
-      }
-      return;
+      cluster_sync();
+      int fn = INT_MAX, fp = INT_MAX;
+      for (int r = 0; r < kCluster; ++r) { fn = min(fn, ctl.rec_nan[r]); fp = min(fp, ctl.rec_pinf[r]); }
+      tok = (fn != INT_MAX) ? fn : (fp != INT_MAX) ? fp : 0;
+    } else {
+      tok = min(R.V - 1, (int)(u * (double)R.V));
     }
-    // only -inf entries: a regular row
-  }
-
-  // ================================================================ GREEDY
-  if (mode == kGreedy) {
-    if (leader && tid == 0) {
-      if (a.out_dtype == NS_OUT_I32) reinterpret_cast<int32_t*>(a.out_tokens)[R.row] = gamax;
-      else reinterpret_cast<int64_t*>(a.out_tokens)[R.row] = gamax;
+    if (leader && tid == 0) write_token(a, R.row, tok);
+    if (debug) {
+      const float pu = 1.0f / (float)R.V;
+      for (int i = tid; i < R.len; i += kThreads) {
+        if (a.out_probs) a.out_probs[out_off + i] = pu;
+        if (a.out_filtered) a.out_filtered[out_off + i] = scaled(R, vals[i]);
+      }
     }
     return;
   }
 
+  // ================================================================ GREEDY
+  if (mode0 == kGreedy) {
+    if (leader && tid == 0) write_token(a, R.row, gamax);
+    return;
+  }
+
   const uint32_t cand_n_addr0 = dsmem_map(smem_addr(&ctl.cand_n), 0);
+  bool need_min = false;
 
   // ================================================================ TOPK
-  if (mode == kTopk) {
-    // bound: lowest key of the bucket holding the k-th largest thread maximum
-    const uint32_t* tm_global = reinterpret_cast<const uint32_t*>(hist) + kTmBins / 2;
+  if (mode0 == kTopk) {
+    const uint32_t* tm_global = hist + kTmBins / 2;
     {
       // thread t owns buckets [kTmBins-8(t+1), kTmBins-8t), scanned from the top
       uint32_t cnt[8];
@@ -779,7 +828,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
         s += cnt[j];
       }
       uint32_t tot;
-      uint32_t pre = block_excl_u32(ctl, s, tot, tid);
+      const uint32_t pre = block_excl_u32(ctl, s, tot, tid);
       if (pre < (uint32_t)R.k && pre + s >= (uint32_t)R.k) {
         uint32_t run = pre;
         for (int j = 0; j < 8; ++j) {
@@ -787,20 +836,23 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
           if (run >= (uint32_t)R.k) { ctl.misc_i = bhi - j; break; }
         }
       }
-      if (tot < (uint32_t)R.k && tid == 0) ctl.misc_i = 0;
+      if (tid == 0 && tot < (uint32_t)R.k) ctl.misc_i = 0;
       __syncthreads();
     }
     const uint32_t bkey = (uint32_t)ctl.misc_i << 20;
     float bound = (bkey < 0x00800000u) ? -INFINITY : key2f(bkey);
     bound = lower_preimage(R, bound);
 
-    // send every element >= bound to the leader (warp-aggregated slots)
+    // every element >= bound goes to the leader (warp-aggregated slots)
     for (int f = R.f_begin + lane; f - lane < R.f_end; f += 32) {
-      float4 v = (f < R.f_end) ? vals4[f] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      const bool live = f < R.f_end;
+      const float4 v = live ? vals4[f] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      const float m4 = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+      if (!__any_sync(0xffffffffu, m4 >= bound)) continue;
       const float t[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const bool take = (f < R.f_end) && (4 * f + c < R.len) && (t[c] >= bound);
+        const bool take = live && (4 * f + c < R.len) && (t[c] >= bound);
         const uint32_t bal = __ballot_sync(0xffffffffu, take);
         if (bal) {
           uint32_t slot0 = 0;
@@ -812,149 +864,153 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
             if (slot < (uint32_t)kCap) {
               dsmem_st_f32(dsmem_map(smem_addr(&cand_s[slot]), 0), scaled(R, t[c]));
               dsmem_st_u32(dsmem_map(smem_addr(&cand_i[slot]), 0), (uint32_t)(R.base + 4 * f + c));
+            } else if (slot == (uint32_t)kCap) {
+              for (int r = 0; r < kCluster; ++r) dsmem_st_u32(dsmem_map(smem_addr(&ctl.overflow), r), 1u);
             }
           }
         }
       }
     }
-    cluster_sync();  // barrier 2: candidates delivered
-    const uint32_t ncand = dsmem_ld_u32(cand_n_addr0);
-    cluster_arrive();  // barrier 3 (arrive): nobody needs the leader's counter afterwards
-    if (ncand <= (uint32_t)kCap) {
+    cluster_sync();  // barrier 2: candidates delivered (and any overflow flagged everywhere)
+    if (!ctl.overflow) {
       if (leader) {
-        const int n = (int)ncand;
-        leader_sort(n, cand_s, cand_i, perm, tid);
-        // top-k threshold and survivors (ties at the threshold are kept)
-        const float s0 = cand_s[perm[0]];
-        const int kk = min(R.k, n);
-        const float thr = cand_s[perm[kk - 1]];
-        if (tid == 0) ctl.misc_i = n;
-        __syncthreads();
-        for (int r = tid; r < n; r += kThreads) {
-          const bool in = cand_s[perm[r]] >= thr;
-          const bool nxt = (r + 1 < n) && (cand_s[perm[r + 1]] >= thr);
-          if (in && !nxt) ctl.misc_i = r + 1;
-        }
-        __syncthreads();
-        const int n1 = ctl.misc_i;
-        for (int r = tid; r < n1; r += kThreads) cand_e[r] = exp_shifted(cand_s[perm[r]], s0);  // e by rank
-        __syncthreads();
-        int n2 = n1;
-        if (R.topp) {
-          if (warp == 0) {
-            uint64_t z = 0;
-            for (int c0 = 0; c0 < n1; c0 += 32) {
-              const int r = c0 + lane;
-              z += warp_u64_sum(r < n1 ? f2fixed(cand_e[r]) : 0ull);
-            }
-            uint64_t run = 0;
-            int j0 = -1;
-            for (int c0 = 0; c0 < n1 && j0 < 0; c0 += 32) {
-              const int r = c0 + lane;
-              const uint64_t fx = r < n1 ? f2fixed(cand_e[r]) : 0ull;
-              const uint64_t inc = warp_incl_u64(fx, lane) + run;
-              const uint32_t bal = __ballot_sync(0xffffffffu, r < n1 && topp_crossed(inc, z, R.p));
-              if (bal) j0 = c0 + __ffs(bal) - 1;
-              run = __shfl_sync(0xffffffffu, inc, 31);
-            }
-            // keep exactly ranks 0..j0 in (value desc, index asc) order
-            if (lane == 0) ctl.misc_i = (j0 >= 0) ? j0 + 1 : n1;
+        const int n = (int)ctl.cand_n;
+        if (n == 0) {  // impossible when the bound holds; keep the kernel total anyway
+          if (tid == 0) write_token(a, R.row, gamax);
+        } else {
+          leader_sort(n, cand_s, cand_i, perm, tid);
+          const float s0 = cand_s[perm[0]];
+          const int kk = min(R.k, n);
+          const float thr = cand_s[perm[kk - 1]];
+          if (tid == 0) { ctl.misc_i = n; ctl.token = INT_MAX; }
+          __syncthreads();
+          for (int r = tid; r < n; r += kThreads) {
+            const bool in = cand_s[perm[r]] >= thr;
+            const bool nxt = (r + 1 < n) && (cand_s[perm[r + 1]] >= thr);
+            if (in && !nxt) ctl.misc_i = r + 1;
           }
           __syncthreads();
-          n2 = ctl.misc_i;
-        }
-        // total kept mass and the inverse-CDF draw in vocabulary order
-        if (warp == 0) {
-          uint64_t z = 0;
-          for (int c0 = 0; c0 < n2; c0 += 32) {
-            const int r = c0 + lane;
-            z += warp_u64_sum(r < n2 ? f2fixed(cand_e[r]) : 0ull);
+          const int n1 = ctl.misc_i;  // survivors of top-k (ties at the threshold kept)
+          for (int r = tid; r < n1; r += kThreads) cand_e[r] = exp_shifted(cand_s[perm[r]], s0);
+          __syncthreads();
+          int n2 = n1;
+          if (R.topp) {
+            if (warp == 0) {
+              double z = 0.0;
+              for (int c0 = 0; c0 < n1; c0 += 32) {
+                const int r = c0 + lane;
+                z += warp_dsum(r < n1 ? (double)cand_e[r] : 0.0);
+              }
+              double run = 0.0;
+              int j0 = -1;
+              for (int c0 = 0; c0 < n1 && j0 < 0; c0 += 32) {
+                const int r = c0 + lane;
+                const double inc = warp_incl_f64(r < n1 ? (double)cand_e[r] : 0.0, lane) + run;
+                const uint32_t bal = __ballot_sync(0xffffffffu, r < n1 && topp_crossed(inc, z, R.p));
+                if (bal) j0 = c0 + __ffs(bal) - 1;
+                run = __shfl_sync(0xffffffffu, inc, 31);
+              }
+              // keep exactly ranks 0..j0 in (value desc, index asc) order
+              if (lane == 0) ctl.misc_i = (j0 >= 0) ? j0 + 1 : n1;
+            }
+            __syncthreads();
+            n2 = ctl.misc_i;
           }
-          if (lane == 0) { ctl.sel_z = z; ctl.token = -1; }
-        }
-        __syncthreads();
-        const uint64_t z2 = ctl.sel_z;
-        const double target = u * (double)z2;
-        for (int r = tid; r < n2; r += kThreads) {
-          const int ir = cand_i[perm[r]];
-          const uint64_t fr = f2fixed(cand_e[r]);
-          uint64_t before = 0;
-          for (int q = 0; q < n2; ++q)
-            if (cand_i[perm[q]] < ir) before += f2fixed(cand_e[q]);
-          if (fr > 0 && (double)before <= target && target < (double)(before + fr)) ctl.token = ir;
-        }
-        __syncthreads();
-        if (tid == 0) {
-          int tok = ctl.token;
-          if (tok < 0) {
-            // target at the very top (rounding): last kept element with mass
-            int last = -1;
-            for (int r = 0; r < n2; ++r)
-              if (f2fixed(cand_e[r]) > 0 && cand_i[perm[r]] > last) last = cand_i[perm[r]];
-            tok = last >= 0 ? last : cand_i[perm[0]];
+          // total kept mass (rank order) and the inverse-CDF draw in vocabulary order
+          if (warp == 0) {
+            double z = 0.0;
+            for (int c0 = 0; c0 < n2; c0 += 32) {
+              const int r = c0 + lane;
+              z += warp_dsum(r < n2 ? (double)cand_e[r] : 0.0);
+            }
+            if (lane == 0) ctl.sel_z = z;
           }
-          if (R.greedy) tok = cand_i[perm[0]];
-          if (a.out_dtype == NS_OUT_I32) reinterpret_cast<int32_t*>(a.out_tokens)[R.row] = tok;
-          else reinterpret_cast<int64_t*>(a.out_tokens)[R.row] = tok;
-          if (debug) {
-            const float thr2 = cand_s[perm[n2 - 1]];
-            const int thr_idx = cand_i[perm[n2 - 1]];
-            for (int r = 0; r < kCluster; ++r) {
-              dsmem_st_f32(dsmem_map(smem_addr(&ctl.bc_thr), r), thr2);
-              dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_thr_idx), r), (uint32_t)thr_idx);
-              dsmem_st_f32(dsmem_map(smem_addr(&ctl.bc_m), r), s0);
-              dsmem_st_f64(dsmem_map(smem_addr(&ctl.bc_z), r), (double)z2 * kFixedToReal);
+          __syncthreads();
+          const double z2 = ctl.sel_z;
+          const double target = u * z2;
+          for (int r = tid; r < n2; r += kThreads) {
+            const int ir = cand_i[perm[r]];
+            const double er = (double)cand_e[r];
+            double before = 0.0;
+            for (int q = 0; q < n2; ++q)
+              if (cand_i[perm[q]] < ir) before += (double)cand_e[q];
+            if (er > 0.0 && before <= target && target < before + er) atomicMin(&ctl.token, ir);
+          }
+          __syncthreads();
+          if (tid == 0) {
+            int tok = ctl.token;
+            if (tok == INT_MAX) {
+              // target at the very top (rounding): the last kept element with mass
+              int last = -1;
+              for (int r = 0; r < n2; ++r)
+                if (cand_e[r] > 0.f && cand_i[perm[r]] > last) last = cand_i[perm[r]];
+              tok = last >= 0 ? last : cand_i[perm[0]];
+            }
+            if (R.greedy) tok = cand_i[perm[0]];
+            write_token(a, R.row, tok);
+            if (debug) {
+              const float thr2 = cand_s[perm[n2 - 1]];
+              const int thr_idx = cand_i[perm[n2 - 1]];
+              for (int r = 0; r < kCluster; ++r) {
+                dsmem_st_f32(dsmem_map(smem_addr(&ctl.bc_thr), r), thr2);
+                dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_thr_idx), r), (uint32_t)thr_idx);
+                dsmem_st_f32(dsmem_map(smem_addr(&ctl.bc_m), r), s0);
+                dsmem_st_f64(dsmem_map(smem_addr(&ctl.bc_z), r), z2);
+              }
             }
           }
         }
       }
-      cluster_wait();  // barrier 3
       if (debug) {
-        cluster_sync();  // barrier 4: leader's broadcast delivered
+        cluster_sync();  // barrier 3: leader's broadcast delivered
         const float thr2 = ctl.bc_thr, m = ctl.bc_m;
         const int thr_idx = ctl.bc_thr_idx;
         const double z = ctl.bc_z;
         for (int i = tid; i < R.len; i += kThreads) {
           const float s = scaled(R, vals[i]);
           const bool kept = s > thr2 || (s == thr2 && R.base + i <= thr_idx);
-          if (a.out_filtered) a.out_filtered[out_row_off + R.base + i] = kept ? s : -INFINITY;
-          if (a.out_probs) a.out_probs[out_row_off + R.base + i] = kept ? (float)((double)exp_shifted(s, m) / z) : 0.0f;
+          if (a.out_filtered) a.out_filtered[out_off + i] = kept ? s : -INFINITY;
+          if (a.out_probs) a.out_probs[out_off + i] = kept ? (float)((double)exp_shifted(s, m) / z) : 0.0f;
         }
       }
       return;
     }
-    // candidate list overflowed: fall back to the general path for this row
-    cluster_wait();  // barrier 3
-    if (leader && tid == 0) set_status(a, NS_STATUS_CAP_OVERFLOW);
-    mode = kGeneral;
-    // the general path needs min-finite; recompute it from the slice
-    float mf = INFINITY;
-    for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
-      const float4 v = vals4[f];
-      float a0 = v.x > -INFINITY ? v.x : INFINITY, a1 = v.y > -INFINITY ? v.y : INFINITY;
-      float a2 = v.z > -INFINITY ? v.z : INFINITY, a3 = v.w > -INFINITY ? v.w : INFINITY;
-      mf = fminf(mf, fminf(fminf(a0, a1), fminf(a2, a3)));
-    }
-    mf = warp_min(mf);
-    if (lane == 0) ctl.red_b[warp] = mf;
-    __syncthreads();
-    if (tid < kCluster) {
-      float m2 = INFINITY;
-      for (int w = 0; w < kWarps; ++w) m2 = fminf(m2, ctl.red_b[w]);
-      dsmem_st_f32(dsmem_map(smem_addr(&ctl.rec_minf[R.rank]), tid), m2);
-    }
-    cluster_sync();
-    gminf = INFINITY;
-    for (int r = 0; r < kCluster; ++r) gminf = fminf(gminf, ctl.rec_minf[r]);
-    if (tid == 0) ctl.cand_n = 0u;
-    __syncthreads();
-    cluster_sync();  // counter reset visible before reuse
+    // the candidate list overflowed: this row takes the general path
+    if (leader && tid == 0 && status) atomicOr(status, NS_STATUS_CAP_OVERFLOW);
+    need_min = true;
   }
 
   // ================================================================ GENERAL
-  const float m = R.t_one ? gmax : __fdiv_rn(gmax, R.T);            // max scaled logit
-  const float minf_s = (gminf < INFINITY) ? (R.t_one ? gminf : __fdiv_rn(gminf, R.T)) : m;
-  int hbuf = 0;  // histogram double-buffer index (for the coarse arrays)
+  if (need_min) {
+    // statistics the TOPK pass did not gather: min and min |x|
+    float mn = INFINITY, amn = INFINITY;
+    for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
+      const float4 v = vals4[f];
+      mn = fminf(mn, fminf(fminf(v.x, v.y), fminf(v.z, v.w)));
+      amn = fminf(amn, fminf(fminf(fabsf(v.x), fabsf(v.y)), fminf(fabsf(v.z), fabsf(v.w))));
+    }
+    mn = warp_min(mn);
+    amn = warp_min(amn);
+    if (lane == 0) { ctl.red_b[warp] = mn; ctl.red_c[warp] = amn; }
+    __syncthreads();
+    if (tid < kCluster) {
+      float m2 = INFINITY, a2 = INFINITY;
+      for (int w = 0; w < kWarps; ++w) { m2 = fminf(m2, ctl.red_b[w]); a2 = fminf(a2, ctl.red_c[w]); }
+      dsmem_st_f32(dsmem_map(smem_addr(&ctl.rec_min[R.rank]), tid), m2);
+      dsmem_st_f32(dsmem_map(smem_addr(&ctl.rec_amin[R.rank]), tid), a2);
+    }
+    if (leader && tid == 0) ctl.cand_n = 0u;
+    cluster_sync();
+    gmin = INFINITY;
+    gamin = INFINITY;
+    for (int r = 0; r < kCluster; ++r) { gmin = fminf(gmin, ctl.rec_min[r]); gamin = fminf(gamin, ctl.rec_amin[r]); }
+  }
+  // The guard-free division needs every |x| of the row in [2^-40, 2^80] and T <= 2^20.
+  const float gabsmax = fmaxf(fabsf(gmax), fabsf(gmin));
+  const bool fast_div = !R.t_one && gamin >= 0x1p-40f && gabsmax <= 0x1p+80f && R.T <= 0x1p+20f;
+  const float m = R.t_one ? gmax : __fdiv_rn(gmax, R.T);  // max scaled logit (division is monotone)
+  const float min_s = (gmin < INFINITY && gmin > -INFINITY) ? (R.t_one ? gmin : __fdiv_rn(gmin, R.T)) : -INFINITY;
+  int hbuf = 0;
 
   // ---- large top-k: exact radix select of the k-th largest penalized logit
   bool have_thr_k = false;
@@ -967,7 +1023,8 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
     for (int lvl = 0; lvl < 3; ++lvl) {
       const int sh = shifts[lvl], wd = widths[lvl];
       const uint32_t nbm = (1u << wd) - 1u;
-      for (int i = tid; i < kBins; i += kThreads) hist[i] = 0ull;
+      uint32_t* h = hist + hbuf * kRadixBins;
+      for (int i = tid; i < kRadixBins; i += kThreads) h[i] = 0u;
       __syncthreads();
       for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
         const float4 v = vals4[f];
@@ -977,246 +1034,248 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
           if (4 * f + c >= R.len) continue;
           const uint32_t key = f2key(t[c]);
           if (lvl > 0 && (key >> (sh + wd)) != prefix) continue;
-          const uint32_t b = nbm - ((key >> sh) & nbm);
-          atomicAdd(reinterpret_cast<unsigned long long*>(&hist[b]), (unsigned long long)kCountOne);
+          atomicAdd(&h[nbm - ((key >> sh) & nbm)], 1u);
         }
       }
       __syncthreads();
-      BucketExp be{0u, 0};
-      cluster_crossing(ctl, hist, hbuf, false, krem, 0ull, 0ull, 0.0f, be, true, tid);
+      radix_crossing(ctl, h, hbuf, krem, tid);
       hbuf ^= 1;
       if (!ctl.sel_found) { ok = false; break; }
       krem -= ctl.sel_before_cnt;
-      prefix = (prefix << wd) | (nbm - (uint32_t)ctl.sel_b);
-      cluster_sync();  // peers done reading this level's histogram
+      prefix = (prefix << wd) | (nbm - (uint32_t)ctl.sel_lo);
     }
     if (ok) {
       have_thr_k = true;
       thr_k_s = scaled(R, key2f(prefix));
     }
+    cluster_sync();  // peers done reading the radix histograms
   }
 
-  // ---- pass 2: e = exp(s - m) in place; top-p mass histogram or draw masses
-  float e_lo_src = have_thr_k ? fmaxf(minf_s, thr_k_s) : minf_s;
-  const float e_lo = exp_shifted(e_lo_src, m);
+  // ---- pass 2: e = exp(s - m) in place; locator histogram; lane masses
+  const float e_lo = exp_shifted(have_thr_k ? fmaxf(min_s, thr_k_s) : min_s, m);
   int SH = 0;
   {
     const uint32_t D = (e_lo > 0.0f) ? (kOne - __float_as_uint(e_lo)) : kOne;
-    while (SH < 18 && (int64_t)(((D + (1u << SH) - 1u) >> SH)) + 1 > kBins - 2) ++SH;
+    while (SH < kMaxShift && (int64_t)((D + (1u << SH) - 1u) >> SH) > kBins - 2) ++SH;
   }
-  uint32_t KC = kOne - 1u + (1u << SH);
-  if (R.topp) {
-    for (int i = tid; i < kBins; i += kThreads) hist[i] = 0ull;
+  const uint32_t KC = kOne - 1u + (1u << SH);
+  const bool topp = R.topp;
+  if (topp) {
+    for (int i = tid; i < kBins / 4; i += kThreads) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
     __syncthreads();
   }
-  float lane_mass = 0.0f;
+  float lane_z = 0.0f;
   for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
     const float4 v = vals4[f];
     float t[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      float e = 0.0f;
-      if (4 * f + c < R.len) {
-        const float s = scaled(R, t[c]);
-        if (!have_thr_k || s >= thr_k_s) e = exp_shifted(s, m);
-      }
+      const float s = R.t_one ? t[c] : (fast_div ? scaled_fast(R, t[c]) : div_by_const(t[c], R.T, R.rT));
+      float e = exp_shifted(s, m);
+      if (have_thr_k && !(s >= thr_k_s)) e = 0.0f;
       t[c] = e;
-      if (R.topp) {
-        if (e > 0.0f) {
-          const uint32_t bits = __float_as_uint(e);
-          const uint32_t b = min((uint32_t)(kBins - 1), (KC - bits) >> SH);
-          atomicAdd(reinterpret_cast<unsigned long long*>(&hist[b]),
-                    (unsigned long long)(kCountOne | (uint64_t)((bits & 0x7fffffu) | 0x800000u)));
-        }
-      } else {
-        lane_mass = __fadd_rn(lane_mass, e);
+      lane_z = __fadd_rn(lane_z, e);
+      if (topp) {
+        const uint32_t bits = __float_as_uint(e);
+        const int d = max(0, (int)(KC - bits));
+        const uint32_t b = min((uint32_t)(kBins - 1), (uint32_t)d >> SH);
+        atomicAdd(&hist[b], approx_mass16(bits));
       }
     }
     vals4[f] = make_float4(t[0], t[1], t[2], t[3]);
   }
-  __syncthreads();
+  {
+    const double cz = cta_warp_sums(ctl, lane_z, lane, warp, tid);  // ctl.wmass = per-warp totals
+    if (tid == 0) ctl.cz[0] = cz;
+    __syncthreads();
+  }
 
-  // ---- top-p: find the crossing bucket, refine, collect, decide
-  float keep_lo = 0.0f;  // kept <=> e >= keep_lo && e > 0
-  if (R.topp) {
-    BucketExp be{KC, SH};
-    uint32_t lo_key = 0, hi_key = 0;
-    uint64_t before = 0, z = 0;
-    bool crossed = false;
-    int lvl = 0;
-    int sh_cur = SH;
-    uint32_t top_cur = KC;
-    for (;;) {
-      cluster_crossing(ctl, hist, hbuf, true, 0u, before, z, R.p, be, lvl > 0, tid);
-      hbuf ^= 1;
-      if (lvl == 0) z = ctl.sel_z;
+  uint32_t keep_lo = 1u;  // kept <=> bits(e) >= keep_lo (1: every positive e)
+  double zkept = 0.0;
+  int owner = -1;
+  double tloc = 0.0;
+  bool crossed = false;
+
+  if (topp) {
+    // ---- top-p locator: a window of buckets that must contain the boundary
+    Level lv{KC, SH, true};
+    uint32_t win_lo = 0, win_hi = 0;
+    topp_window(ctl, hist, 0, lv, true, 0.0, R.p, tid);
+    const double z = ctl.sel_z;
+    for (int lvl = 0;; ++lvl) {
       if (!ctl.sel_found) break;
-      const int B = ctl.sel_b;
-      before += ctl.sel_before_mass;
-      lo_key = top_cur - (uint32_t)(B + 1) * (1u << sh_cur) + 1u;
-      hi_key = top_cur - (uint32_t)B * (1u << sh_cur);
+      win_lo = lv.lo_key(ctl.sel_hi);
+      win_hi = lv.hi_key(ctl.sel_lo);
       crossed = true;
-      const uint32_t cnt = ctl.sel_cnt;
-      if (cnt <= (uint32_t)kCap || sh_cur == 0 || lvl >= 3) break;
-      // refine inside [lo_key, hi_key]
-      cluster_sync();  // peers done reading this level's histogram
-      const int sh_next = max(0, sh_cur - 11);
-      for (int i = tid; i < kBins; i += kThreads) hist[i] = 0ull;
+      if (ctl.sel_est <= 0.9f * (float)kCap || lv.sh == 0 || lvl >= 2) break;
+      // refine inside [win_lo, win_hi]: finer buckets, exact mass above the window
+      const uint32_t span = win_hi - win_lo + 1u;
+      int sh2 = 0;
+      while (((span + (1u << sh2) - 1u) >> sh2) > (uint32_t)(kBins - 1)) ++sh2;
+      if (sh2 >= lv.sh) sh2 = lv.sh - 1;
+      cluster_sync();  // peers done reading this level's histogram and sums
+      for (int i = tid; i < kBins / 4; i += kThreads) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
       __syncthreads();
+      float lane_above = 0.0f;
       for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
         const float4 v = vals4[f];
         const float t[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const uint32_t bits = __float_as_uint(t[c]);
-          if (t[c] > 0.0f && bits >= lo_key && bits <= hi_key) {
-            const uint32_t b = (hi_key - bits) >> sh_next;
-            atomicAdd(reinterpret_cast<unsigned long long*>(&hist[b]),
-                      (unsigned long long)(kCountOne | (uint64_t)((bits & 0x7fffffu) | 0x800000u)));
+          if (bits > win_hi) lane_above = __fadd_rn(lane_above, t[c]);
+          else if (bits >= win_lo) atomicAdd(&hist[(win_hi - bits) >> sh2], approx_mass16(bits));
+        }
+      }
+      {
+        const double s = cta_warp_sums(ctl, lane_above, lane, warp, tid);
+        if (tid == 0) ctl.cz[1] = s;
+        __syncthreads();
+      }
+      lv = Level{win_hi, sh2, false};
+      topp_window(ctl, hist, 1, lv, false, z, R.p, tid);
+    }
+    cluster_sync();  // peers done reading the locator histograms
+    if (crossed) {
+      // ---- collection: exact mass above the window; window members -> leader
+      float lane_above = 0.0f;
+      for (int f = R.f_begin + lane; f - lane < R.f_end; f += 32) {
+        const bool live = f < R.f_end;
+        const float4 v = live ? vals4[f] : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float t[4] = {v.x, v.y, v.z, v.w};
+        bool any_mem = false;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t bits = __float_as_uint(t[c]);
+          if (bits > win_hi) lane_above = __fadd_rn(lane_above, t[c]);
+          any_mem |= (bits >= win_lo && bits <= win_hi);
+        }
+        if (!__any_sync(0xffffffffu, any_mem)) continue;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t bits = __float_as_uint(t[c]);
+          const bool take = live && bits >= win_lo && bits <= win_hi;
+          const uint32_t bal = __ballot_sync(0xffffffffu, take);
+          if (bal) {
+            uint32_t slot0 = 0;
+            const int first = __ffs(bal) - 1;
+            if (lane == first) slot0 = dsmem_atom_add_u32(cand_n_addr0, (uint32_t)__popc(bal));
+            slot0 = __shfl_sync(0xffffffffu, slot0, first);
+            if (take) {
+              const uint32_t slot = slot0 + (uint32_t)__popc(bal & ((1u << lane) - 1u));
+              const int local = 4 * f + c;
+              const float s = scaled(R, penalized_from_global(R, bitmap, local));
+              if (slot < (uint32_t)kCap) {
+                dsmem_st_f32(dsmem_map(smem_addr(&cand_s[slot]), 0), s);
+                dsmem_st_u32(dsmem_map(smem_addr(&cand_i[slot]), 0), (uint32_t)(R.base + local));
+                dsmem_st_f32(dsmem_map(smem_addr(&cand_e[slot]), 0), t[c]);
+              }
+              const uint32_t ms = atomicAdd(&ctl.mem_n, 1u);
+              if (ms < (uint32_t)kCap) { mem_s[ms] = s; mem_i[ms] = local; }
+            }
           }
+        }
+      }
+      {
+        const double s = cta_warp_sums(ctl, lane_above, lane, warp, tid);  // ctl.wmass = above masses
+        if (tid == 0) dsmem_st_f64(dsmem_map(smem_addr(&ctl.rec_above[R.rank]), 0), s);
+      }
+      cluster_sync();  // barrier: members and above-window masses delivered
+      if (leader) {
+        const uint32_t ntot = ctl.cand_n;
+        const int n = (int)min(ntot, (uint32_t)kCap);
+        leader_sort(n, cand_s, cand_i, perm, tid);
+        if (warp == 0) {
+          double before = 0.0;
+          for (int r = 0; r < kCluster; ++r) before += ctl.rec_above[r];
+          int j0 = -1;
+          double run = before;
+          if (ntot <= (uint32_t)kCap) {
+            for (int c0 = 0; c0 < n && j0 < 0; c0 += 32) {
+              const int r = c0 + lane;
+              const float er = r < n ? cand_e[perm[r]] : 0.f;
+              const double inc = warp_incl_f64((double)er, lane) + run;
+              const uint32_t bal = __ballot_sync(0xffffffffu, r < n && er > 0.f && topp_crossed(inc, z, R.p));
+              if (bal) j0 = c0 + __ffs(bal) - 1;
+              run = __shfl_sync(0xffffffffu, inc, 31);
+            }
+          }
+          if (j0 < 0) j0 = n - 1;  // no crossing inside (or overflow): keep the window
+          const float thr = n > 0 ? cand_s[perm[j0]] : -INFINITY;
+          const int thr_idx = n > 0 ? cand_i[perm[j0]] : INT_MAX;
+          // kept mass per CTA: above-window mass + kept members (rank order)
+          double kept[kCluster];
+#pragma unroll
+          for (int r = 0; r < kCluster; ++r) kept[r] = ctl.rec_above[r];
+          for (int r = 0; r <= j0 && r < n; ++r) {
+            const int owner_r = cand_i[perm[r]] / R.W;
+            const double add = (double)cand_e[perm[r]];
+#pragma unroll
+            for (int q = 0; q < kCluster; ++q)
+              if (q == owner_r) kept[q] += add;
+          }
+          double zk = 0.0;
+#pragma unroll
+          for (int r = 0; r < kCluster; ++r) zk += kept[r];
+          int own;
+          double t_own = 0.0;
+          pick_owner(kept, u * zk, own, t_own);
+          if (lane < kCluster) {
+            const uint32_t r = (uint32_t)lane;
+            dsmem_st_f32(dsmem_map(smem_addr(&ctl.bc_thr), r), thr);
+            dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_thr_idx), r), (uint32_t)thr_idx);
+            dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_owner), r), (uint32_t)own);
+            dsmem_st_f64(dsmem_map(smem_addr(&ctl.bc_tloc), r), t_own);
+            dsmem_st_f64(dsmem_map(smem_addr(&ctl.bc_z), r), zk);
+          }
+          if (ntot > (uint32_t)kCap && lane == 0 && status) atomicOr(status, NS_STATUS_CAP_OVERFLOW);
+        }
+      }
+      cluster_sync();  // barrier: decision delivered
+      const float thr = ctl.bc_thr;
+      const int thr_idx = ctl.bc_thr_idx;
+      owner = ctl.bc_owner;
+      tloc = ctl.bc_tloc;
+      zkept = ctl.bc_z;
+      // drop this CTA's members ranked after the threshold element; add the
+      // kept ones to the per-warp masses (fixed point: order-independent)
+      if (tid < kWarps) ctl.wfix[tid] = 0ull;
+      __syncthreads();
+      const int nm = (int)min(ctl.mem_n, (uint32_t)kCap);
+      for (int i = tid; i < nm; i += kThreads) {
+        const float sm = mem_s[i];
+        const int li = mem_i[i];
+        if (sm < thr || (sm == thr && R.base + li > thr_idx)) {
+          vals[li] = 0.0f;
+        } else {
+          const int w = min(kWarps - 1, (li >> 2) / R.chunk);
+          atomicAdd(&ctl.wfix[w], (unsigned long long)llrint((double)vals[li] * kFixedScale));
         }
       }
       __syncthreads();
-      sh_cur = sh_next;
-      top_cur = hi_key;
-      be = BucketExp{hi_key, sh_next};
-      ++lvl;
+      if (tid < kWarps) ctl.wmass[tid] += (double)ctl.wfix[tid] * kFixedToReal;
+      __syncthreads();
+      keep_lo = win_lo;
     }
-    if (!crossed) {
-      keep_lo = 0.0f;  // the mass never passes top_p: keep everything
-      cluster_sync();
-    } else {
-      cluster_sync();  // peers done reading the last histogram; leader counter is zero
-      const uint32_t total_cnt = ctl.sel_cnt;
-      const bool collect = total_cnt <= (uint32_t)kCap;
-      if (collect) {
-        // members of the crossing bucket -> leader (exact s recomputed from global)
-        for (int f = R.f_begin + lane; f - lane < R.f_end; f += 32) {
-          const float4 v = (f < R.f_end) ? vals4[f] : make_float4(0.f, 0.f, 0.f, 0.f);
-          const float t[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint32_t bits = __float_as_uint(t[c]);
-            const bool take = (f < R.f_end) && t[c] > 0.0f && bits >= lo_key && bits <= hi_key;
-            const uint32_t bal = __ballot_sync(0xffffffffu, take);
-            if (bal) {
-              uint32_t slot0 = 0;
-              const int first = __ffs(bal) - 1;
-              if (lane == first) slot0 = dsmem_atom_add_u32(cand_n_addr0, (uint32_t)__popc(bal));
-              slot0 = __shfl_sync(0xffffffffu, slot0, first);
-              if (take) {
-                const uint32_t slot = slot0 + (uint32_t)__popc(bal & ((1u << lane) - 1u));
-                const int local = 4 * f + c;
-                const float s = scaled(R, penalized_from_global(R, bitmap, local));
-                if (slot < (uint32_t)kCap) {
-                  dsmem_st_f32(dsmem_map(smem_addr(&cand_s[slot]), 0), s);
-                  dsmem_st_u32(dsmem_map(smem_addr(&cand_i[slot]), 0), (uint32_t)(R.base + local));
-                  dsmem_st_f32(dsmem_map(smem_addr(&cand_e[slot]), 0), t[c]);
-                }
-                const uint32_t ms = atomicAdd(&ctl.mem_n, 1u);
-                if (ms < (uint32_t)kCap) { mem_s[ms] = s; mem_i[ms] = local; }
-              }
-            }
-          }
-        }
-      }
-      cluster_sync();  // barrier: members delivered
-      if (leader && collect) {
-        const int n = (int)min(ctl.cand_n, (uint32_t)kCap);
-        leader_sort(n, cand_s, cand_i, perm, tid);
-        if (warp == 0) {
-          uint64_t run = before;
-          int j0 = -1;
-          for (int c0 = 0; c0 < n && j0 < 0; c0 += 32) {
-            const int r = c0 + lane;
-            const uint64_t fx = r < n ? f2fixed(cand_e[perm[r]]) : 0ull;
-            const uint64_t inc = warp_incl_u64(fx, lane) + run;
-            const uint32_t bal = __ballot_sync(0xffffffffu, r < n && fx > 0 && topp_crossed(inc, z, R.p));
-            if (bal) j0 = c0 + __ffs(bal) - 1;
-            run = __shfl_sync(0xffffffffu, inc, 31);
-          }
-          if (lane == 0) {
-            // rank j0 in (value desc, index asc) order is the last one kept
-            const float thr = (j0 >= 0) ? cand_s[perm[j0]] : -INFINITY;
-            const int thr_idx = (j0 >= 0) ? cand_i[perm[j0]] : INT_MAX;
-            for (int r = 0; r < kCluster; ++r) {
-              dsmem_st_f32(dsmem_map(smem_addr(&ctl.bc_thr), r), thr);
-              dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_thr_idx), r), (uint32_t)thr_idx);
-              dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_flag), r), 1u);
-            }
-          }
-        }
-      }
-      if (!collect && leader && tid == 0) set_status(a, NS_STATUS_CAP_OVERFLOW);
-      cluster_sync();  // barrier: decision delivered
-      if (collect && ctl.bc_flag) {
-        // drop this CTA's members ranked after the threshold element
-        const float thr = ctl.bc_thr;
-        const int thr_idx = ctl.bc_thr_idx;
-        const int nm = (int)min(ctl.mem_n, (uint32_t)kCap);
-        for (int i = tid; i < nm; i += kThreads) {
-          const float sm = mem_s[i];
-          if (sm < thr || (sm == thr && R.base + mem_i[i] > thr_idx)) vals[mem_i[i]] = 0.0f;
-        }
-        __syncthreads();
-      }
-      keep_lo = __uint_as_float(lo_key);
-    }
-    // per-lane kept mass
-    lane_mass = 0.0f;
-    for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
-      const float4 v = vals4[f];
-      lane_mass = __fadd_rn(lane_mass, (v.x >= keep_lo && v.x > 0.f) ? v.x : 0.f);
-      lane_mass = __fadd_rn(lane_mass, (v.y >= keep_lo && v.y > 0.f) ? v.y : 0.f);
-      lane_mass = __fadd_rn(lane_mass, (v.z >= keep_lo && v.z > 0.f) ? v.z : 0.f);
-      lane_mass = __fadd_rn(lane_mass, (v.w >= keep_lo && v.w > 0.f) ? v.w : 0.f);
-    }
+  }
+  if (!topp || !crossed) {
+    // plain sampling, large top-k alone, or a top-p that never crosses: draw over all e
+    if (tid < kCluster) dsmem_st_f64(dsmem_map(smem_addr(&ctl.rec_z[R.rank]), tid), ctl.cz[0]);
+    cluster_sync();
+    for (int r = 0; r < kCluster; ++r) zkept += ctl.rec_z[r];
+    pick_owner(ctl.rec_z, u * zkept, owner, tloc);
+    keep_lo = 1u;
   }
 
-  // ---- CTA masses -> every CTA
-  {
-    const double wm = warp_dsum((double)lane_mass);
-    if (lane == 0) ctl.wmass[warp] = wm;
-    __syncthreads();
-    if (tid < kCluster) {
-      double cm = 0.0;
-      for (int w = 0; w < kWarps; ++w) cm += ctl.wmass[w];
-      dsmem_st_f64(dsmem_map(smem_addr(&ctl.rec_mass[R.rank]), tid), cm);
-    }
-  }
-  cluster_sync();  // barrier: masses delivered
-
-  double ztot = 0.0;
-  for (int r = 0; r < kCluster; ++r) ztot += ctl.rec_mass[r];
-  const double target = u * ztot;
-  int owner = -1;
-  double pre_owner = 0.0;
-  {
-    double run = 0.0;
-    int last_pos = -1;
-    double last_pre = 0.0;
-    for (int r = 0; r < kCluster; ++r) {
-      const double mr = ctl.rec_mass[r];
-      if (mr > 0.0) { last_pos = r; last_pre = run; }
-      if (owner < 0 && mr > 0.0 && run + mr > target) { owner = r; pre_owner = run; }
-      run += mr;
-    }
-    if (owner < 0) { owner = last_pos; pre_owner = last_pre; }
-  }
-  if (R.greedy) {
-    if (leader && tid == 0) {
-      if (a.out_dtype == NS_OUT_I32) reinterpret_cast<int32_t*>(a.out_tokens)[R.row] = gamax;
-      else reinterpret_cast<int64_t*>(a.out_tokens)[R.row] = gamax;
-    }
+  // ---- the draw: the owning CTA walks its warps' kept masses in vocabulary order
+  if (R.greedy || owner < 0) {
+    if (leader && tid == 0) write_token(a, R.row, gamax);
   } else if ((int)R.rank == owner) {
-    // owning warp
-    double tloc = target - pre_owner;
     int wsel = -1;
     double wpre = 0.0;
     {
-      double run = 0.0;
+      double run = 0.0, lastpre = 0.0;
       int lastw = -1;
-      double lastpre = 0.0;
       for (int w = 0; w < kWarps; ++w) {
         const double x = ctl.wmass[w];
         if (x > 0.0) { lastw = w; lastpre = run; }
@@ -1236,12 +1295,11 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
           const float4 v = vals4[f];
           const float t[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-          for (int c = 0; c < 4; ++c) q[c] = (t[c] >= keep_lo && t[c] > 0.f) ? t[c] : 0.f;
+          for (int c = 0; c < 4; ++c) q[c] = (__float_as_uint(t[c]) >= keep_lo && t[c] > 0.f) ? t[c] : 0.f;
         }
         const float ls = __fadd_rn(__fadd_rn(__fadd_rn(q[0], q[1]), q[2]), q[3]);
         const double inc = warp_incl_f64((double)ls, lane);
         const double rowtot = __shfl_sync(0xffffffffu, inc, 31);
-        // last kept element seen so far (for the clamp)
         int lk = -1;
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -1272,21 +1330,18 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
       }
       if (tok < 0) tok = last_kept;
       if (tok < 0) tok = gamax;  // no kept mass at all (cannot happen for a regular row)
-      if (lane == 0) {
-        if (a.out_dtype == NS_OUT_I32) reinterpret_cast<int32_t*>(a.out_tokens)[R.row] = tok;
-        else reinterpret_cast<int64_t*>(a.out_tokens)[R.row] = tok;
-      }
+      if (lane == 0) write_token(a, R.row, tok);
     }
   }
   if (debug) {
     for (int i = tid; i < R.len; i += kThreads) {
       const float e = vals[i];
-      const bool kept = (e >= keep_lo && e > 0.f);
-      if (a.out_probs) a.out_probs[out_row_off + R.base + i] = kept ? (float)((double)e / ztot) : 0.0f;
+      const bool kept = __float_as_uint(e) >= keep_lo && e > 0.f;
+      if (a.out_probs) a.out_probs[out_off + i] = kept ? (float)((double)e / zkept) : 0.0f;
       if (a.out_filtered) {
         float sv = -INFINITY;
         if (kept) sv = scaled(R, penalized_from_global(R, bitmap, i));
-        a.out_filtered[out_row_off + R.base + i] = sv;
+        a.out_filtered[out_off + i] = sv;
       }
     }
   }
@@ -1307,7 +1362,7 @@ std::mutex g_mu;
 DeviceState g_dev[64];
 
 int slice_width(int V) {
-  int W = (V + kCluster - 1) / kCluster;
+  const int W = (V + kCluster - 1) / kCluster;
   return (W + 7) & ~7;
 }
 

@@ -75,7 +75,8 @@ void sample_op(const at::Tensor& logits, const c10::optional<at::Tensor>& sample
   a.logits_dtype = logits.scalar_type() == at::kFloat ? NS_DTYPE_F32 : NS_DTYPE_BF16;
   a.vocab_size = (int32_t)V;
   a.num_logit_rows = logits.size(0);
-  a.logits_row_stride = logits.stride(0);
+  // a single-row tensor may report any stride for its size-1 dimension
+  a.logits_row_stride = logits.size(0) == 1 ? V : logits.stride(0);
   a.num_rows = (int32_t)S;
   a.out_dtype = out.scalar_type() == at::kLong ? NS_OUT_I64 : NS_OUT_I32;
   a.sample_indices = static_cast<const int64_t*>(opt_ptr(sample_indices));

@@ -54,7 +54,7 @@ def run_cabi(logits: torch.Tensor, params, histories, uniforms: Optional[np.ndar
     a.logits_dtype = cabi.NS_DTYPE_BF16 if logits.dtype == torch.bfloat16 else cabi.NS_DTYPE_F32
     a.vocab_size = V
     a.num_logit_rows = logits.shape[0]
-    a.logits_row_stride = logits.stride(0)
+    a.logits_row_stride = V if logits.shape[0] == 1 else logits.stride(0)
     a.num_rows = S
     a.out_dtype = cabi.NS_OUT_I32 if out_i32 else cabi.NS_OUT_I64
     a.sample_indices = si.data_ptr() if si is not None else None
