@@ -110,6 +110,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Orders this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (bulk copy) accesses to the same shared memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 // Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
 // global memory into this CTA's shared memory; completion is counted on `bar`.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -2,23 +2,28 @@
 //
 // Replaces nanoserve/scheduler/sampler.py:21-89 (Sampler.sample).  Design:
 //
-//  * One thread-block cluster of kCluster (8) CTAs per sampled row.  CTA r
-//    owns the contiguous vocabulary slice [r*W, r*W+W) and keeps it in its
-//    shared memory for the whole step, so the row crosses HBM exactly once.
-//    Each warp pulls its own contiguous piece of the slice with one
-//    mbarrier-tracked bulk copy (cp.async.bulk, no multicast) and starts
-//    working on it as soon as it lands.
+//  * Persistent thread-block clusters of kCluster (8) CTAs, as many as are
+//    co-resident (two CTAs per SM); cluster c samples rows c, c+G, c+2G...
+//    CTA r of a cluster owns the contiguous vocabulary slice [r*W, r*W+W)
+//    of the current row and keeps it in its shared memory while it needs
+//    it, so every row crosses HBM exactly once.  Each warp moves its own
+//    contiguous piece of the slice with one mbarrier-tracked bulk copy
+//    (cp.async.bulk, global -> own shared memory, no multicast) and issues
+//    the copy for the NEXT row as soon as it has finished reading the
+//    current one, so HBM keeps streaming while the cluster exchanges
+//    statistics, waits at barriers and decides.
 //  * Row statistics, histograms and candidate lists are exchanged through
 //    distributed shared memory (st/ld/red/atom .shared::cluster) between
-//    cluster barriers.  No global scratch memory is used.
+//    cluster barriers.  Areas that peers write into are double-buffered by
+//    row parity.  No global scratch memory is used.
 //  * Three row paths, chosen per row (uniformly across the cluster):
 //      GREEDY   temperature == 0 and no debug output: first-index argmax
 //               (sampler.py:82-83); one exchange.
 //      TOPK     0 < top_k <= kTopkSmall: a histogram of per-thread maxima
 //               bounds the k-th largest logit from below; every element
-//               above the bound goes to the leader CTA, which finishes top-k
-//               (sampler.py:53-58), top-p (sampler.py:60-73), softmax and the
-//               inverse-CDF draw on that short list.
+//               above the bound goes to the row's leader CTA, which
+//               finishes top-k (sampler.py:53-58), top-p (sampler.py:60-73),
+//               softmax and the inverse-CDF draw on that short list.
 //      GENERAL  anything else: exp(s - max) is computed once per element and
 //               kept in place.  Top-p locates its boundary with a histogram
 //               of approximate masses keyed on the bits of exp(s - max)
@@ -54,17 +59,16 @@ constexpr int kRadixBins = 2048;     // radix-select level histogram (u32 counts
 constexpr int kRadixCoarse = 32;
 constexpr int kCap = 512;            // leader candidate list capacity
 constexpr int kTopkSmall = 128;      // largest top_k served by the TOPK path
-constexpr int kTmBins = 4096;        // per-thread-maximum histogram (u16 counts)
+constexpr int kTmBins = 2048;        // per-thread-maximum histogram (u16 counts), quarter binades
+constexpr int kTmShift = 21;
 constexpr int kMaxSlice = 24576;     // largest slice (elements) one CTA holds
 constexpr int kMaxShift = 17;        // locator buckets cover >= 63.9 binades of exp(s - max)
 constexpr uint32_t kOne = 0x3F800000u;           // bits of 1.0f
 constexpr double kWindowSlack = 1.0 + 0x1p-14;  // > 1 / (1 - 2^-15): locator mass error bound
 constexpr double kFixedScale = 17592186044416.0;  // 2^44
 
-// Fixed-size control block at the start of dynamic shared memory.
-struct __align__(16) Ctl {
-  uint64_t mbar[kWarps];
-  // per-peer records (slot = peer rank), written by the peers
+// What peers write into this CTA during one row; double-buffered by row parity.
+struct __align__(16) Recv {
   float rec_max[kCluster];
   float rec_min[kCluster];
   float rec_amin[kCluster];
@@ -73,13 +77,19 @@ struct __align__(16) Ctl {
   int32_t rec_pinf[kCluster];
   double rec_z[kCluster];
   double rec_above[kCluster];
-  // own coarse sums, double-buffered (peers read them)
+  uint32_t cand_n;
+  uint32_t overflow;
+  uint32_t pad[2];
+  uint32_t tm_global[kTmBins / 2];
+};
+
+// Fixed-size control block at the start of dynamic shared memory.
+struct __align__(16) Ctl {
+  uint64_t mbar[kWarps];
+  // own coarse sums, double-buffered by level (peers read them)
   double cmass[2][kCoarse];
   uint32_t ccnt[2][kRadixCoarse];
   double cz[2];
-  // leader candidate list control (peers add to it)
-  uint32_t cand_n;
-  uint32_t overflow;
   // leader broadcast
   float bc_thr;
   int32_t bc_thr_idx;
@@ -110,7 +120,7 @@ struct __align__(16) Ctl {
 };
 
 struct Layout {
-  size_t ctl, hist, bitmap, cand_s, cand_i, cand_e, perm, mem_s, mem_i, vals, total;
+  size_t ctl, recv, hist, bitmap, cand_s, cand_i, cand_e, perm, mem_s, mem_i, mem_e, vals, total;
 };
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
@@ -119,6 +129,7 @@ __host__ __device__ inline Layout make_layout(int W) {
   Layout L;
   size_t o = 0;
   L.ctl = o;    o = align16(o + sizeof(Ctl));
+  L.recv = o;   o = align16(o + 2 * sizeof(Recv));
   L.hist = o;   o = align16(o + sizeof(uint32_t) * kBins);
   L.bitmap = o; o = align16(o + sizeof(uint32_t) * ((W + 31) / 32));
   L.cand_s = o; o = align16(o + sizeof(float) * kCap);
@@ -127,6 +138,7 @@ __host__ __device__ inline Layout make_layout(int W) {
   L.perm = o;   o = align16(o + sizeof(int32_t) * kCap);
   L.mem_s = o;  o = align16(o + sizeof(float) * kCap);
   L.mem_i = o;  o = align16(o + sizeof(int32_t) * kCap);
+  L.mem_e = o;  o = align16(o + sizeof(float) * kCap);
   L.vals = o;   o = align16(o + sizeof(float) * W);
   L.total = o;
   return L;
@@ -181,27 +193,50 @@ __device__ __forceinline__ bool topp_crossed(double cum, double z, float p) {
   return (float)(cum / z) > p;
 }
 
-// ---------------------------------------------------------------- per-row context
-struct Row {
-  int row, V, W, base, len, nf4, full4, f_begin, f_end, chunk;
+// ---------------------------------------------------------------- contexts
+// Where logits rows come from (copied out of the kernel parameters).
+struct Src {
+  const void* logits;
+  const int64_t* sidx;
+  int64_t nrows;
+  int64_t stride;
+  bool bf16;
+};
+__device__ __forceinline__ int64_t source_row(const Src& S, int row, bool& bad) {
+  int64_t src = row;
+  bad = false;
+  if (S.sidx) src = S.sidx[row];
+  if (src < 0 || src >= S.nrows) { bad = true; src = 0; }
+  return src;
+}
+
+// The CTA's slice geometry (the same for every row).
+struct Geo {
+  int V, W, base, len, nf4, full4, chunk, f_begin, f_end;
   uint32_t rank;
+  bool tma, vec16;
+};
+
+// One row being sampled.
+struct Row {
+  int row;
+  uint32_t lead;  // the row's leader CTA
   const float* src32;
   const __nv_bfloat16* src16;
-  bool tma, vec16;
   float T, rT;
   bool t_one, greedy, topp, pen;
   int k;
   float p, rp;
 };
 
-__device__ __forceinline__ float load_scalar(const Row& R, int local) {
-  if (R.src16) return __bfloat162float(R.src16[R.base + local]);
-  return R.src32[R.base + local];
+__device__ __forceinline__ float load_scalar(const Geo& g, const Row& R, int local) {
+  if (R.src16) return __bfloat162float(R.src16[g.base + local]);
+  return R.src32[g.base + local];
 }
 // Logit after the repetition penalty for one element of this CTA's slice,
-// re-read from global memory (candidate recomputation and debug outputs).
-__device__ __forceinline__ float penalized_from_global(const Row& R, const uint32_t* bitmap, int local) {
-  float x = load_scalar(R, local);
+// re-read from global memory.
+__device__ __forceinline__ float penalized_from_global(const Geo& g, const Row& R, const uint32_t* bitmap, int local) {
+  float x = load_scalar(g, R, local);
   if (R.pen && ((bitmap[local >> 5] >> (local & 31)) & 1u)) x = penalize(x, R.rp);
   return x;
 }
@@ -220,15 +255,15 @@ __device__ __forceinline__ float scaled_fast(const Row& R, float x) {
 // store it to shared memory when it did not arrive there by bulk copy or was
 // changed, and emit the penalized debug output.  Elements past the slice end
 // read as -inf.
-__device__ __forceinline__ float4 load_slot(const Row& R, float* vals, const uint32_t* bitmap, int f,
+__device__ __forceinline__ float4 load_slot(const Geo& g, const Row& R, float* vals, const uint32_t* bitmap, int f,
                                             float* pen_out) {
   float4 v;
   const int e0 = f * 4;
   bool dirty = false;
-  if (R.tma && f < R.full4) {
+  if (g.tma && f < g.full4) {
     v = reinterpret_cast<const float4*>(vals)[f];
-  } else if (R.vec16 && e0 + 3 < R.len) {
-    uint2 raw = *reinterpret_cast<const uint2*>(R.src16 + R.base + e0);
+  } else if (g.vec16 && e0 + 3 < g.len) {
+    uint2 raw = *reinterpret_cast<const uint2*>(R.src16 + g.base + e0);
     __nv_bfloat162 lo = *reinterpret_cast<__nv_bfloat162*>(&raw.x);
     __nv_bfloat162 hi = *reinterpret_cast<__nv_bfloat162*>(&raw.y);
     float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
@@ -237,7 +272,7 @@ __device__ __forceinline__ float4 load_slot(const Row& R, float* vals, const uin
   } else {
     float t[4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) t[c] = (e0 + c < R.len) ? load_scalar(R, e0 + c) : -INFINITY;
+    for (int c = 0; c < 4; ++c) t[c] = (e0 + c < g.len) ? load_scalar(g, R, e0 + c) : -INFINITY;
     v = make_float4(t[0], t[1], t[2], t[3]);
     dirty = true;
   }
@@ -256,17 +291,35 @@ __device__ __forceinline__ float4 load_slot(const Row& R, float* vals, const uin
     const float t[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int c = 0; c < 4; ++c)
-      if (e0 + c < R.len) pen_out[e0 + c] = t[c];
+      if (e0 + c < g.len) pen_out[e0 + c] = t[c];
   }
   return v;
 }
 
-// Bounded wait for this warp's bulk copy.  On give-up the status word is set
-// and the kernel carries on, so that no cluster barrier is left waiting.
-__device__ __forceinline__ void wait_my_copy(const Row& R, Ctl& ctl, int warp, uint32_t* status) {
-  if (!R.tma || R.f_begin >= min(R.f_end, R.full4)) return;
+// Issue this warp's bulk copy of row `row` into its piece of the slice.
+// The warp must be done reading and writing that piece for the current row.
+__device__ __forceinline__ void issue_chunk(const Src& S, const Geo& g, Ctl& ctl, float* vals, int row, int warp,
+                                            int lane) {
+  __syncwarp();
+  if (!g.tma || lane != 0) return;
+  const int fe = min(g.f_end, g.full4);
+  if (fe <= g.f_begin) return;
+  bool bad;
+  const int64_t src = source_row(S, row, bad);
+  const float* p = reinterpret_cast<const float*>(S.logits) + src * S.stride + g.base + 4 * g.f_begin;
+  const uint32_t bytes = (uint32_t)(fe - g.f_begin) * 16u;
+  fence_proxy_async_smem();
+  mbar_arrive_expect_tx(&ctl.mbar[warp], bytes);
+  bulk_g2s(vals + 4 * g.f_begin, p, bytes, &ctl.mbar[warp]);
+}
+
+// Bounded wait for this warp's bulk copy of the current row.  On give-up the
+// status word is set and the kernel carries on, so that no cluster barrier
+// is left waiting.
+__device__ __forceinline__ void wait_chunk(const Geo& g, Ctl& ctl, int warp, uint32_t parity, uint32_t* status) {
+  if (!g.tma || g.f_begin >= min(g.f_end, g.full4)) return;
   uint32_t spins = 0;
-  while (!mbar_try_wait(&ctl.mbar[warp], 0)) {
+  while (!mbar_try_wait(&ctl.mbar[warp], parity)) {
     if (++spins > (1u << 22)) {
       if (status) atomicOr(status, NS_STATUS_WAIT_TIMEOUT);
       break;
@@ -288,9 +341,9 @@ __device__ float lower_preimage(const Row& R, float b) {
   return -INFINITY;
 }
 
-__device__ __forceinline__ void write_token(const NsSampleArgs& a, int row, int tok) {
-  if (a.out_dtype == NS_OUT_I32) reinterpret_cast<int32_t*>(a.out_tokens)[row] = tok;
-  else reinterpret_cast<int64_t*>(a.out_tokens)[row] = tok;
+__device__ __forceinline__ void write_token(void* out, bool i32, int row, int tok) {
+  if (i32) reinterpret_cast<int32_t*>(out)[row] = tok;
+  else reinterpret_cast<int64_t*>(out)[row] = tok;
 }
 
 // Block-wide exclusive scan of one u32 per thread (thread 0 first).
@@ -380,7 +433,7 @@ struct Level {
   __device__ __forceinline__ uint32_t lo_key(int b) const { return top - (uint32_t)(b + 1) * (1u << sh) + 1u; }
   __device__ __forceinline__ uint32_t hi_key(int b) const { return top - (uint32_t)b * (1u << sh); }
   __device__ __forceinline__ double mass(uint32_t sum16, int b) const {
-    if (last_is_overflow && b == kBins - 1) return 0.0;
+    if (sum16 == 0u || (last_is_overflow && b == kBins - 1)) return 0.0;
     const int ex = (int)(lo_key(b) >> 23);
     return ldexp((double)sum16, ex - 142);
   }
@@ -505,18 +558,17 @@ __device__ void leader_sort(int n, const float* cs, const int32_t* ci, int32_t* 
   __syncthreads();
 }
 
-// Per-warp sums of lane values and their total over the CTA (fixed order).
-__device__ __forceinline__ double cta_warp_sums(Ctl& ctl, float lane_v, int lane, int warp, int tid) {
+// Per-warp sums of lane values (into ctl.wmass) and their CTA total.
+__device__ __forceinline__ double cta_warp_sums(Ctl& ctl, float lane_v, int lane, int warp) {
   const double w = warp_dsum((double)lane_v);
   if (lane == 0) ctl.wmass[warp] = w;
   __syncthreads();
   double s = 0.0;
   for (int i = 0; i < kWarps; ++i) s += ctl.wmass[i];
-  (void)tid;
   return s;
 }
 
-// Owner of global row r's mass: first CTA whose mass prefix passes target.
+// First CTA whose mass prefix passes target, and the target within it.
 __device__ __forceinline__ void pick_owner(const double* m, double target, int& owner, double& tloc) {
   double run = 0.0, last_pre = 0.0;
   int last = -1;
@@ -530,156 +582,163 @@ __device__ __forceinline__ void pick_owner(const double* m, double target, int& 
   if (owner < 0) { owner = last; tloc = target - last_pre; }
 }
 
-// ---------------------------------------------------------------- the kernel
-__global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs a, int W, int tma_ok, int vec16_ok) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  const Layout L = make_layout(W);
-  Ctl& ctl = *reinterpret_cast<Ctl*>(smem + L.ctl);
-  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + L.hist);
-  uint32_t* bitmap = reinterpret_cast<uint32_t*>(smem + L.bitmap);
-  float* cand_s = reinterpret_cast<float*>(smem + L.cand_s);
-  int32_t* cand_i = reinterpret_cast<int32_t*>(smem + L.cand_i);
-  float* cand_e = reinterpret_cast<float*>(smem + L.cand_e);
-  int32_t* perm = reinterpret_cast<int32_t*>(smem + L.perm);
-  float* mem_s = reinterpret_cast<float*>(smem + L.mem_s);
-  int32_t* mem_i = reinterpret_cast<int32_t*>(smem + L.mem_i);
-  float* vals = reinterpret_cast<float*>(smem + L.vals);
-  float4* vals4 = reinterpret_cast<float4*>(vals);
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  Row R;
-  R.rank = cluster_ctarank();
-  R.row = blockIdx.x / kCluster;
-  R.V = a.vocab_size;
-  R.W = W;
-  R.base = (int)R.rank * W;
-  R.len = max(0, min(W, R.V - R.base));
-  R.nf4 = (R.len + 3) >> 2;
-  R.full4 = R.len >> 2;
-  R.chunk = max(1, (R.nf4 + kWarps - 1) / kWarps);
-  R.f_begin = min(R.nf4, warp * R.chunk);
-  R.f_end = min(R.nf4, R.f_begin + R.chunk);
-  const bool leader = (R.rank == 0);
-  uint32_t* const status = a.status;
-
-  // source row (fused gather of sample_indices)
-  int64_t src = R.row;
-  bool bad_row = false;
-  if (a.sample_indices) {
-    src = a.sample_indices[R.row];
-    if (src < 0 || src >= a.num_logit_rows) { bad_row = true; src = 0; }
-  } else if (src >= a.num_logit_rows) {
-    bad_row = true;
-    src = 0;
+// What the owner warp needs to recompute kept masses from global memory.
+struct Keep {
+  float m;             // max scaled logit
+  bool have_thr_k;     // large top-k mask: s >= thr_k_s
+  float thr_k_s;
+  bool window;         // top-p window decision
+  uint32_t win_lo, win_hi;
+  float thr;           // last kept (s, idx) inside the window
+  int thr_idx;
+};
+__device__ __forceinline__ float kept_mass(const Geo& g, const Row& R, const Keep& K, const uint32_t* bitmap,
+                                           int local) {
+  if (local >= g.len) return 0.f;
+  const float s = scaled(R, penalized_from_global(g, R, bitmap, local));
+  if (K.have_thr_k && !(s >= K.thr_k_s)) return 0.f;
+  const float e = exp_shifted(s, K.m);
+  if (!(e > 0.f)) return 0.f;
+  if (K.window) {
+    const uint32_t bits = __float_as_uint(e);
+    if (bits < K.win_lo) return 0.f;
+    if (bits <= K.win_hi && (s < K.thr || (s == K.thr && g.base + local > K.thr_idx))) return 0.f;
   }
-  if (a.logits_dtype == NS_DTYPE_BF16) {
-    R.src16 = reinterpret_cast<const __nv_bfloat16*>(a.logits) + src * a.logits_row_stride;
+  return e;
+}
+
+// ---------------------------------------------------------------- one row
+struct Shared {
+  Ctl* ctl;
+  Recv* recv;
+  uint32_t* hist;
+  uint32_t* bitmap;
+  float* cand_s;
+  int32_t* cand_i;
+  float* cand_e;
+  int32_t* perm;
+  float* mem_s;
+  int32_t* mem_i;
+  float* mem_e;
+  float* vals;
+};
+
+// Samples `row`.  Every path issues this warp's bulk copy of `next_row` as
+// soon as the warp has finished with its piece of the slice and records that
+// in `prefetched`; the caller issues it at the end of the row otherwise.
+__device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S, const Geo& g, const Shared& sm,
+                                            int row, int next_row, uint32_t par, int tid, bool& prefetched) {
+  const int lane = tid & 31, warp = tid >> 5;
+  Ctl& ctl = *sm.ctl;
+  Recv& rv = sm.recv[par];
+  uint32_t* hist = sm.hist;
+  uint32_t* bitmap = sm.bitmap;
+  float* vals = sm.vals;
+  float4* vals4 = reinterpret_cast<float4*>(vals);
+  uint32_t* const status = a.status;
+  prefetched = false;
+  auto prefetch = [&]() {
+    if (!prefetched) {
+      prefetched = true;
+      if (next_row >= 0) issue_chunk(S, g, ctl, vals, next_row, warp, lane);
+    }
+  };
+
+  Row R;
+  R.row = row;
+  R.lead = (uint32_t)(row & (kCluster - 1));
+  const bool leader = (g.rank == R.lead);
+  bool bad_row;
+  const int64_t src = source_row(S, row, bad_row);
+  if (S.bf16) {
+    R.src16 = reinterpret_cast<const __nv_bfloat16*>(S.logits) + src * S.stride;
     R.src32 = nullptr;
   } else {
-    R.src32 = reinterpret_cast<const float*>(a.logits) + src * a.logits_row_stride;
+    R.src32 = reinterpret_cast<const float*>(S.logits) + src * S.stride;
     R.src16 = nullptr;
   }
-  R.tma = tma_ok && R.src32 != nullptr;
-  R.vec16 = vec16_ok && R.src16 != nullptr;
-
-  const NsRowParams P = a.row_params[R.row];
+  const NsRowParams P = a.row_params[row];
   R.greedy = (P.flags & NS_ROW_GREEDY) != 0u;
   R.T = R.greedy ? 1.0f : P.temperature;
   R.rT = __frcp_rn(R.T);
   R.t_one = (R.T == 1.0f);
   R.topp = (P.flags & NS_ROW_TOP_P) != 0u;
   R.p = P.top_p;
-  R.k = (P.top_k > 0 && P.top_k < R.V) ? P.top_k : 0;
+  R.k = (P.top_k > 0 && P.top_k < g.V) ? P.top_k : 0;
   R.rp = P.repetition_penalty;
   int64_t h0 = 0, h1 = 0;
   if (a.history_offsets && (P.flags & NS_ROW_PENALTY)) {
-    h0 = a.history_offsets[R.row];
-    h1 = a.history_offsets[R.row + 1];
+    h0 = a.history_offsets[row];
+    h1 = a.history_offsets[row + 1];
   }
   R.pen = (P.flags & NS_ROW_PENALTY) != 0u && h1 > h0;
   const bool debug = (a.out_filtered != nullptr) || (a.out_probs != nullptr);
-  const int64_t out_off = (int64_t)R.row * R.V + R.base;
+  const int64_t out_off = (int64_t)row * g.V + g.base;
   float* pen_out = a.out_penalized ? a.out_penalized + out_off : nullptr;
+  const bool out_i32 = (a.out_dtype == NS_OUT_I32);
 
   enum { kGreedy, kTopk, kGeneral };
   const int mode0 = (R.greedy && !debug) ? kGreedy : (R.k > 0 && R.k <= kTopkSmall) ? kTopk : kGeneral;
 
-  // ---------------- setup: barriers, zeroed histograms, penalty bitmap
-  if (tid == 0) {
-    for (int w = 0; w < kWarps; ++w) mbar_init(&ctl.mbar[w], 1);
-    fence_mbar_init();
-    ctl.cand_n = 0u;
-    ctl.overflow = 0u;
-    ctl.mem_n = 0u;
-  }
+  // ---------------- per-row setup (the caller synchronised the CTA)
+  if (tid == 0) ctl.mem_n = 0u;
   for (int i = tid; i < kBins / 4; i += kThreads) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
-  if (R.pen)
-    for (int i = tid; i < (W + 31) / 32; i += kThreads) bitmap[i] = 0u;
-  __syncthreads();
-  cluster_arrive();  // barrier 0: every CTA's shared memory is initialised
-
-  // each warp fetches its own piece of the slice
-  if (R.tma && lane == 0) {
-    const int fe = min(R.f_end, R.full4);
-    if (fe > R.f_begin) {
-      const uint32_t bytes = (uint32_t)(fe - R.f_begin) * 16u;
-      mbar_arrive_expect_tx(&ctl.mbar[warp], bytes);
-      bulk_g2s(vals + 4 * R.f_begin, R.src32 + R.base + 4 * R.f_begin, bytes, &ctl.mbar[warp]);
-    }
-  }
   if (R.pen) {
+    for (int i = tid; i < (g.W + 31) / 32; i += kThreads) bitmap[i] = 0u;
+    __syncthreads();
     uint32_t bad = 0;
     for (int64_t i = h0 + tid; i < h1; i += kThreads) {
       const int id = a.history_ids[i];
-      if (id < 0 || id >= R.V) { bad = 1; continue; }
-      const int local = id - R.base;
-      if (local >= 0 && local < R.len) atomicOr(&bitmap[local >> 5], 1u << (local & 31));
+      if (id < 0 || id >= g.V) { bad = 1; continue; }
+      const int local = id - g.base;
+      if (local >= 0 && local < g.len) atomicOr(&bitmap[local >> 5], 1u << (local & 31));
     }
     if (bad && leader && status) atomicOr(status, NS_STATUS_BAD_HISTORY_ID);
-    __syncthreads();
   }
+  __syncthreads();
   if (bad_row && leader && tid == 0 && status) atomicOr(status, NS_STATUS_BAD_SAMPLE_INDEX);
-
-  wait_my_copy(R, ctl, warp, status);
 
   // row uniform
   double u;
   if (a.uniforms) {
-    u = (double)a.uniforms[R.row];
+    u = (double)a.uniforms[row];
   } else {
     const uint64_t key = (P.flags & NS_ROW_SEED) ? P.seed : a.philox_seed;
-    u = philox_uniform(key, a.philox_offset, (uint64_t)(a.row_offset + R.row));
+    u = philox_uniform(key, a.philox_offset, (uint64_t)(a.row_offset + row));
   }
   if (!(u >= 0.0)) u = 0.0;
   if (u >= 1.0) u = 0x1.fffffffffffffp-1;
+
+  wait_chunk(g, ctl, warp, par, status);
 
   // ---------------- pass 1 (mode-specific statistics)
   float st_max = -INFINITY, st_min = INFINITY, st_amin = INFINITY;
   int st_amax = INT_MAX;
   if (mode0 == kTopk && !R.greedy) {
-    for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
-      const float4 v = load_slot(R, vals, bitmap, f, pen_out);
+    for (int f = g.f_begin + lane; f < g.f_end; f += 32) {
+      const float4 v = load_slot(g, R, vals, bitmap, f, pen_out);
       st_max = fmax_nan(st_max, fmax_nan(fmax_nan(v.x, v.y), fmax_nan(v.z, v.w)));
     }
   } else {
     const bool want_min = (mode0 == kGeneral);
     const bool want_amin = want_min && !R.t_one;
-    for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
-      const float4 v = load_slot(R, vals, bitmap, f, pen_out);
+    for (int f = g.f_begin + lane; f < g.f_end; f += 32) {
+      const float4 v = load_slot(g, R, vals, bitmap, f, pen_out);
       const float m4 = fmax_nan(fmax_nan(v.x, v.y), fmax_nan(v.z, v.w));
       if (m4 > st_max) {
         const int c = (v.x == m4) ? 0 : (v.y == m4) ? 1 : (v.z == m4) ? 2 : 3;
-        st_amax = R.base + 4 * f + c;
+        st_amax = g.base + 4 * f + c;
       }
       st_max = fmax_nan(st_max, m4);
       if (want_min) st_min = fminf(st_min, fminf(fminf(v.x, v.y), fminf(v.z, v.w)));
       if (want_amin)
         st_amin = fminf(st_amin, fminf(fminf(fabsf(v.x), fabsf(v.y)), fminf(fabsf(v.z), fabsf(v.w))));
     }
+    if (mode0 == kGreedy) prefetch();  // the slice is no longer needed
   }
   if (mode0 == kTopk) {
     // local histogram of thread maxima (u16 counts packed in u32 words)
-    const uint32_t b = f2key(st_max) >> 20;
+    const uint32_t b = f2key(st_max) >> kTmShift;
     atomicAdd(&hist[b >> 1], 1u << ((b & 1u) << 4));
   }
   // CTA reduction of (max with NaN propagation, argmax, min, min |x|)
@@ -698,7 +757,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
       ctl.red_c[warp] = vamin;
     }
     __syncthreads();
-    if (tid == 0) {
+    if (tid < kCluster) {
       float m = -INFINITY, mn = INFINITY, amn = INFINITY;
       int mi = INT_MAX;
       bool nan_any = false;
@@ -710,35 +769,18 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
         mn = fminf(mn, ctl.red_b[w]);
         amn = fminf(amn, ctl.red_c[w]);
       }
-      ctl.red_a[0] = nan_any ? __int_as_float(0x7fc00000) : m;
-      ctl.red_i[0] = mi;
-      ctl.red_b[0] = mn;
-      ctl.red_c[0] = amn;
+      const uint32_t r = (uint32_t)tid;
+      dsmem_st_f32(dsmem_map(smem_addr(&rv.rec_max[g.rank]), r), nan_any ? __int_as_float(0x7fc00000) : m);
+      dsmem_st_f32(dsmem_map(smem_addr(&rv.rec_min[g.rank]), r), mn);
+      dsmem_st_f32(dsmem_map(smem_addr(&rv.rec_amin[g.rank]), r), amn);
+      dsmem_st_u32(dsmem_map(smem_addr(&rv.rec_amax[g.rank]), r), (uint32_t)mi);
     }
-    __syncthreads();
-  }
-  const float cta_max = ctl.red_a[0];
-  const int cta_amax = ctl.red_i[0];
-  const float cta_min = ctl.red_b[0];
-  const float cta_amin = ctl.red_c[0];
-  __syncthreads();
-
-  cluster_wait();  // barrier 0 complete: peers may now be written
-
-  if (tid < kCluster) {
-    const uint32_t r = (uint32_t)tid;
-    dsmem_st_f32(dsmem_map(smem_addr(&ctl.rec_max[R.rank]), r), cta_max);
-    dsmem_st_f32(dsmem_map(smem_addr(&ctl.rec_min[R.rank]), r), cta_min);
-    dsmem_st_f32(dsmem_map(smem_addr(&ctl.rec_amin[R.rank]), r), cta_amin);
-    dsmem_st_u32(dsmem_map(smem_addr(&ctl.rec_amax[R.rank]), r), (uint32_t)cta_amax);
   }
   if (mode0 == kTopk) {
-    const uint32_t* tm_local = hist;
-    uint32_t* tm_global = hist + kTmBins / 2;
     for (int w = tid; w < kTmBins / 2; w += kThreads) {
-      const uint32_t v = tm_local[w];
+      const uint32_t v = hist[w];
       if (v) {
-        const uint32_t ad = smem_addr(&tm_global[w]);
+        const uint32_t ad = smem_addr(&rv.tm_global[w]);
 #pragma unroll
         for (int r = 0; r < kCluster; ++r) dsmem_red_add_u32(dsmem_map(ad, r), v);
       }
@@ -750,31 +792,26 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
   int gamax = INT_MAX;
   bool gnan = false;
   for (int r = 0; r < kCluster; ++r) {
-    const float x = ctl.rec_max[r];
+    const float x = rv.rec_max[r];
     if (x != x) gnan = true;
-    else if (x > gmax) { gmax = x; gamax = ctl.rec_amax[r]; }
-    gmin = fminf(gmin, ctl.rec_min[r]);
-    gamin = fminf(gamin, ctl.rec_amin[r]);
+    else if (x > gmax) { gmax = x; gamax = rv.rec_amax[r]; }
+    gmin = fminf(gmin, rv.rec_min[r]);
+    gamin = fminf(gamin, rv.rec_amin[r]);
   }
   if (gmax == -INFINITY) gamax = 0;
 
   // ---------------- rows whose softmax is NaN: uniform 1/V (sampler.py:76-80)
   if (gnan || gmax == INFINITY || gmax == -INFINITY) {
+    prefetch();
     int tok = 0;
     if (R.greedy) {
-      // torch.argmax: the first NaN, else the first +inf, else index 0
+      // torch.argmax: the first NaN, else the first +inf, else index 0.  The
+      // penalty keeps NaN and +inf, so the raw logits in global memory decide.
       int my_nan = INT_MAX, my_pinf = INT_MAX;
-      for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
-        const float4 v = vals4[f];
-        const float t[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (4 * f + c < R.len) {
-            const int idx = R.base + 4 * f + c;
-            if (t[c] != t[c]) my_nan = min(my_nan, idx);
-            if (t[c] == INFINITY) my_pinf = min(my_pinf, idx);
-          }
-        }
+      for (int i = tid; i < g.len; i += kThreads) {
+        const float x = load_scalar(g, R, i);
+        if (x != x) my_nan = min(my_nan, g.base + i);
+        if (x == INFINITY) my_pinf = min(my_pinf, g.base + i);
       }
       my_nan = warp_imin(my_nan);
       my_pinf = warp_imin(my_pinf);
@@ -783,22 +820,22 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
       if (tid < kCluster) {
         int n = INT_MAX, q = INT_MAX;
         for (int w = 0; w < kWarps; ++w) { n = min(n, ctl.red_i[w]); q = min(q, ctl.red_j[w]); }
-        dsmem_st_u32(dsmem_map(smem_addr(&ctl.rec_nan[R.rank]), tid), (uint32_t)n);
-        dsmem_st_u32(dsmem_map(smem_addr(&ctl.rec_pinf[R.rank]), tid), (uint32_t)q);
+        dsmem_st_u32(dsmem_map(smem_addr(&rv.rec_nan[g.rank]), tid), (uint32_t)n);
+        dsmem_st_u32(dsmem_map(smem_addr(&rv.rec_pinf[g.rank]), tid), (uint32_t)q);
       }
       cluster_sync();
       int fn = INT_MAX, fp = INT_MAX;
-      for (int r = 0; r < kCluster; ++r) { fn = min(fn, ctl.rec_nan[r]); fp = min(fp, ctl.rec_pinf[r]); }
+      for (int r = 0; r < kCluster; ++r) { fn = min(fn, rv.rec_nan[r]); fp = min(fp, rv.rec_pinf[r]); }
       tok = (fn != INT_MAX) ? fn : (fp != INT_MAX) ? fp : 0;
     } else {
-      tok = min(R.V - 1, (int)(u * (double)R.V));
+      tok = min(g.V - 1, (int)(u * (double)g.V));
     }
-    if (leader && tid == 0) write_token(a, R.row, tok);
+    if (leader && tid == 0) write_token(a.out_tokens, out_i32, row, tok);
     if (debug) {
-      const float pu = 1.0f / (float)R.V;
-      for (int i = tid; i < R.len; i += kThreads) {
+      const float pu = 1.0f / (float)g.V;
+      for (int i = tid; i < g.len; i += kThreads) {
         if (a.out_probs) a.out_probs[out_off + i] = pu;
-        if (a.out_filtered) a.out_filtered[out_off + i] = scaled(R, vals[i]);
+        if (a.out_filtered) a.out_filtered[out_off + i] = scaled(R, penalized_from_global(g, R, bitmap, i));
       }
     }
     return;
@@ -806,32 +843,31 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
 
   // ================================================================ GREEDY
   if (mode0 == kGreedy) {
-    if (leader && tid == 0) write_token(a, R.row, gamax);
+    if (leader && tid == 0) write_token(a.out_tokens, out_i32, row, gamax);
     return;
   }
 
-  const uint32_t cand_n_addr0 = dsmem_map(smem_addr(&ctl.cand_n), 0);
+  const uint32_t cand_n_lead = dsmem_map(smem_addr(&rv.cand_n), R.lead);
   bool need_min = false;
 
   // ================================================================ TOPK
   if (mode0 == kTopk) {
-    const uint32_t* tm_global = hist + kTmBins / 2;
     {
-      // thread t owns buckets [kTmBins-8(t+1), kTmBins-8t), scanned from the top
-      uint32_t cnt[8];
+      // thread t owns buckets [kTmBins-4(t+1), kTmBins-4t), scanned from the top
+      uint32_t cnt[4];
       uint32_t s = 0;
-      const int bhi = kTmBins - 1 - 8 * tid;
+      const int bhi = kTmBins - 1 - 4 * tid;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 4; ++j) {
         const int b = bhi - j;
-        cnt[j] = (tm_global[b >> 1] >> ((b & 1) << 4)) & 0xFFFFu;
+        cnt[j] = (rv.tm_global[b >> 1] >> ((b & 1) << 4)) & 0xFFFFu;
         s += cnt[j];
       }
       uint32_t tot;
       const uint32_t pre = block_excl_u32(ctl, s, tot, tid);
       if (pre < (uint32_t)R.k && pre + s >= (uint32_t)R.k) {
         uint32_t run = pre;
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < 4; ++j) {
           run += cnt[j];
           if (run >= (uint32_t)R.k) { ctl.misc_i = bhi - j; break; }
         }
@@ -839,44 +875,49 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
       if (tid == 0 && tot < (uint32_t)R.k) ctl.misc_i = 0;
       __syncthreads();
     }
-    const uint32_t bkey = (uint32_t)ctl.misc_i << 20;
+    const uint32_t bkey = (uint32_t)ctl.misc_i << kTmShift;
     float bound = (bkey < 0x00800000u) ? -INFINITY : key2f(bkey);
     bound = lower_preimage(R, bound);
 
     // every element >= bound goes to the leader (warp-aggregated slots)
-    for (int f = R.f_begin + lane; f - lane < R.f_end; f += 32) {
-      const bool live = f < R.f_end;
+    for (int f = g.f_begin + lane; f - lane < g.f_end; f += 32) {
+      const bool live = f < g.f_end;
       const float4 v = live ? vals4[f] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
       const float m4 = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
       if (!__any_sync(0xffffffffu, m4 >= bound)) continue;
       const float t[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const bool take = live && (4 * f + c < R.len) && (t[c] >= bound);
+        const bool take = live && (4 * f + c < g.len) && (t[c] >= bound);
         const uint32_t bal = __ballot_sync(0xffffffffu, take);
         if (bal) {
           uint32_t slot0 = 0;
           const int first = __ffs(bal) - 1;
-          if (lane == first) slot0 = dsmem_atom_add_u32(cand_n_addr0, (uint32_t)__popc(bal));
+          if (lane == first) slot0 = dsmem_atom_add_u32(cand_n_lead, (uint32_t)__popc(bal));
           slot0 = __shfl_sync(0xffffffffu, slot0, first);
           if (take) {
             const uint32_t slot = slot0 + (uint32_t)__popc(bal & ((1u << lane) - 1u));
             if (slot < (uint32_t)kCap) {
-              dsmem_st_f32(dsmem_map(smem_addr(&cand_s[slot]), 0), scaled(R, t[c]));
-              dsmem_st_u32(dsmem_map(smem_addr(&cand_i[slot]), 0), (uint32_t)(R.base + 4 * f + c));
+              dsmem_st_f32(dsmem_map(smem_addr(&sm.cand_s[slot]), R.lead), scaled(R, t[c]));
+              dsmem_st_u32(dsmem_map(smem_addr(&sm.cand_i[slot]), R.lead), (uint32_t)(g.base + 4 * f + c));
             } else if (slot == (uint32_t)kCap) {
-              for (int r = 0; r < kCluster; ++r) dsmem_st_u32(dsmem_map(smem_addr(&ctl.overflow), r), 1u);
+              for (int r = 0; r < kCluster; ++r) dsmem_st_u32(dsmem_map(smem_addr(&rv.overflow), r), 1u);
             }
           }
         }
       }
     }
     cluster_sync();  // barrier 2: candidates delivered (and any overflow flagged everywhere)
-    if (!ctl.overflow) {
+    if (!rv.overflow) {
+      prefetch();
       if (leader) {
-        const int n = (int)ctl.cand_n;
-        if (n == 0) {  // impossible when the bound holds; keep the kernel total anyway
-          if (tid == 0) write_token(a, R.row, gamax);
+        const int n = (int)rv.cand_n;
+        float* cand_s = sm.cand_s;
+        int32_t* cand_i = sm.cand_i;
+        float* cand_e = sm.cand_e;
+        int32_t* perm = sm.perm;
+        if (n == 0) {  // impossible while the bound holds; keep the kernel total anyway
+          if (tid == 0) write_token(a.out_tokens, out_i32, row, gamax);
         } else {
           leader_sort(n, cand_s, cand_i, perm, tid);
           const float s0 = cand_s[perm[0]];
@@ -947,7 +988,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
               tok = last >= 0 ? last : cand_i[perm[0]];
             }
             if (R.greedy) tok = cand_i[perm[0]];
-            write_token(a, R.row, tok);
+            write_token(a.out_tokens, out_i32, row, tok);
             if (debug) {
               const float thr2 = cand_s[perm[n2 - 1]];
               const int thr_idx = cand_i[perm[n2 - 1]];
@@ -966,9 +1007,9 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
         const float thr2 = ctl.bc_thr, m = ctl.bc_m;
         const int thr_idx = ctl.bc_thr_idx;
         const double z = ctl.bc_z;
-        for (int i = tid; i < R.len; i += kThreads) {
-          const float s = scaled(R, vals[i]);
-          const bool kept = s > thr2 || (s == thr2 && R.base + i <= thr_idx);
+        for (int i = tid; i < g.len; i += kThreads) {
+          const float s = scaled(R, penalized_from_global(g, R, bitmap, i));
+          const bool kept = s > thr2 || (s == thr2 && g.base + i <= thr_idx);
           if (a.out_filtered) a.out_filtered[out_off + i] = kept ? s : -INFINITY;
           if (a.out_probs) a.out_probs[out_off + i] = kept ? (float)((double)exp_shifted(s, m) / z) : 0.0f;
         }
@@ -984,7 +1025,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
   if (need_min) {
     // statistics the TOPK pass did not gather: min and min |x|
     float mn = INFINITY, amn = INFINITY;
-    for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
+    for (int f = g.f_begin + lane; f < g.f_end; f += 32) {
       const float4 v = vals4[f];
       mn = fminf(mn, fminf(fminf(v.x, v.y), fminf(v.z, v.w)));
       amn = fminf(amn, fminf(fminf(fabsf(v.x), fabsf(v.y)), fminf(fabsf(v.z), fabsf(v.w))));
@@ -996,25 +1037,30 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
     if (tid < kCluster) {
       float m2 = INFINITY, a2 = INFINITY;
       for (int w = 0; w < kWarps; ++w) { m2 = fminf(m2, ctl.red_b[w]); a2 = fminf(a2, ctl.red_c[w]); }
-      dsmem_st_f32(dsmem_map(smem_addr(&ctl.rec_min[R.rank]), tid), m2);
-      dsmem_st_f32(dsmem_map(smem_addr(&ctl.rec_amin[R.rank]), tid), a2);
+      dsmem_st_f32(dsmem_map(smem_addr(&rv.rec_min[g.rank]), tid), m2);
+      dsmem_st_f32(dsmem_map(smem_addr(&rv.rec_amin[g.rank]), tid), a2);
     }
-    if (leader && tid == 0) ctl.cand_n = 0u;
+    if (leader && tid == 0) rv.cand_n = 0u;
     cluster_sync();
     gmin = INFINITY;
     gamin = INFINITY;
-    for (int r = 0; r < kCluster; ++r) { gmin = fminf(gmin, ctl.rec_min[r]); gamin = fminf(gamin, ctl.rec_amin[r]); }
+    for (int r = 0; r < kCluster; ++r) { gmin = fminf(gmin, rv.rec_min[r]); gamin = fminf(gamin, rv.rec_amin[r]); }
   }
   // The guard-free division needs every |x| of the row in [2^-40, 2^80] and T <= 2^20.
   const float gabsmax = fmaxf(fabsf(gmax), fabsf(gmin));
   const bool fast_div = !R.t_one && gamin >= 0x1p-40f && gabsmax <= 0x1p+80f && R.T <= 0x1p+20f;
-  const float m = R.t_one ? gmax : __fdiv_rn(gmax, R.T);  // max scaled logit (division is monotone)
+  Keep K;
+  K.m = R.t_one ? gmax : __fdiv_rn(gmax, R.T);  // max scaled logit (division is monotone)
+  K.have_thr_k = false;
+  K.thr_k_s = -INFINITY;
+  K.window = false;
+  K.win_lo = K.win_hi = 0u;
+  K.thr = -INFINITY;
+  K.thr_idx = INT_MAX;
   const float min_s = (gmin < INFINITY && gmin > -INFINITY) ? (R.t_one ? gmin : __fdiv_rn(gmin, R.T)) : -INFINITY;
   int hbuf = 0;
 
   // ---- large top-k: exact radix select of the k-th largest penalized logit
-  bool have_thr_k = false;
-  float thr_k_s = -INFINITY;
   if (R.k > 0) {
     uint32_t prefix = 0, krem = (uint32_t)R.k;
     const int shifts[3] = {21, 10, 0};
@@ -1026,12 +1072,12 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
       uint32_t* h = hist + hbuf * kRadixBins;
       for (int i = tid; i < kRadixBins; i += kThreads) h[i] = 0u;
       __syncthreads();
-      for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
+      for (int f = g.f_begin + lane; f < g.f_end; f += 32) {
         const float4 v = vals4[f];
         const float t[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          if (4 * f + c >= R.len) continue;
+          if (4 * f + c >= g.len) continue;
           const uint32_t key = f2key(t[c]);
           if (lvl > 0 && (key >> (sh + wd)) != prefix) continue;
           atomicAdd(&h[nbm - ((key >> sh) & nbm)], 1u);
@@ -1045,14 +1091,14 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
       prefix = (prefix << wd) | (nbm - (uint32_t)ctl.sel_lo);
     }
     if (ok) {
-      have_thr_k = true;
-      thr_k_s = scaled(R, key2f(prefix));
+      K.have_thr_k = true;
+      K.thr_k_s = scaled(R, key2f(prefix));
     }
     cluster_sync();  // peers done reading the radix histograms
   }
 
   // ---- pass 2: e = exp(s - m) in place; locator histogram; lane masses
-  const float e_lo = exp_shifted(have_thr_k ? fmaxf(min_s, thr_k_s) : min_s, m);
+  const float e_lo = exp_shifted(K.have_thr_k ? fmaxf(min_s, K.thr_k_s) : min_s, K.m);
   int SH = 0;
   {
     const uint32_t D = (e_lo > 0.0f) ? (kOne - __float_as_uint(e_lo)) : kOne;
@@ -1065,32 +1111,36 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
     __syncthreads();
   }
   float lane_z = 0.0f;
-  for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
-    const float4 v = vals4[f];
-    float t[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const float s = R.t_one ? t[c] : (fast_div ? scaled_fast(R, t[c]) : div_by_const(t[c], R.T, R.rT));
-      float e = exp_shifted(s, m);
-      if (have_thr_k && !(s >= thr_k_s)) e = 0.0f;
-      t[c] = e;
-      lane_z = __fadd_rn(lane_z, e);
-      if (topp) {
-        const uint32_t bits = __float_as_uint(e);
-        const int d = max(0, (int)(KC - bits));
-        const uint32_t b = min((uint32_t)(kBins - 1), (uint32_t)d >> SH);
-        atomicAdd(&hist[b], approx_mass16(bits));
-      }
-    }
-    vals4[f] = make_float4(t[0], t[1], t[2], t[3]);
-  }
   {
-    const double cz = cta_warp_sums(ctl, lane_z, lane, warp, tid);  // ctl.wmass = per-warp totals
+    const float m = K.m, thr_k_s = K.thr_k_s;
+    const bool have_thr_k = K.have_thr_k;
+    for (int f = g.f_begin + lane; f < g.f_end; f += 32) {
+      const float4 v = vals4[f];
+      float t[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float s = R.t_one ? t[c] : (fast_div ? scaled_fast(R, t[c]) : div_by_const(t[c], R.T, R.rT));
+        float e = exp_shifted(s, m);
+        if (have_thr_k && !(s >= thr_k_s)) e = 0.0f;
+        t[c] = e;
+        lane_z = __fadd_rn(lane_z, e);
+        if (topp) {
+          const uint32_t bits = __float_as_uint(e);
+          const int d = max(0, (int)(KC - bits));
+          const uint32_t b = min((uint32_t)(kBins - 1), (uint32_t)d >> SH);
+          atomicAdd(&hist[b], approx_mass16(bits));
+        }
+      }
+      if (topp) vals4[f] = make_float4(t[0], t[1], t[2], t[3]);
+    }
+  }
+  if (!topp) prefetch();  // the draw recomputes its masses from global memory
+  {
+    const double cz = cta_warp_sums(ctl, lane_z, lane, warp);  // ctl.wmass = per-warp totals
     if (tid == 0) ctl.cz[0] = cz;
     __syncthreads();
   }
 
-  uint32_t keep_lo = 1u;  // kept <=> bits(e) >= keep_lo (1: every positive e)
   double zkept = 0.0;
   int owner = -1;
   double tloc = 0.0;
@@ -1117,7 +1167,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
       for (int i = tid; i < kBins / 4; i += kThreads) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
       __syncthreads();
       float lane_above = 0.0f;
-      for (int f = R.f_begin + lane; f < R.f_end; f += 32) {
+      for (int f = g.f_begin + lane; f < g.f_end; f += 32) {
         const float4 v = vals4[f];
         const float t[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -1128,7 +1178,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
         }
       }
       {
-        const double s = cta_warp_sums(ctl, lane_above, lane, warp, tid);
+        const double s = cta_warp_sums(ctl, lane_above, lane, warp);
         if (tid == 0) ctl.cz[1] = s;
         __syncthreads();
       }
@@ -1136,11 +1186,12 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
       topp_window(ctl, hist, 1, lv, false, z, R.p, tid);
     }
     cluster_sync();  // peers done reading the locator histograms
+    if (!crossed) prefetch();
     if (crossed) {
       // ---- collection: exact mass above the window; window members -> leader
       float lane_above = 0.0f;
-      for (int f = R.f_begin + lane; f - lane < R.f_end; f += 32) {
-        const bool live = f < R.f_end;
+      for (int f = g.f_begin + lane; f - lane < g.f_end; f += 32) {
+        const bool live = f < g.f_end;
         const float4 v = live ? vals4[f] : make_float4(0.f, 0.f, 0.f, 0.f);
         const float t[4] = {v.x, v.y, v.z, v.w};
         bool any_mem = false;
@@ -1159,35 +1210,40 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
           if (bal) {
             uint32_t slot0 = 0;
             const int first = __ffs(bal) - 1;
-            if (lane == first) slot0 = dsmem_atom_add_u32(cand_n_addr0, (uint32_t)__popc(bal));
+            if (lane == first) slot0 = dsmem_atom_add_u32(cand_n_lead, (uint32_t)__popc(bal));
             slot0 = __shfl_sync(0xffffffffu, slot0, first);
             if (take) {
               const uint32_t slot = slot0 + (uint32_t)__popc(bal & ((1u << lane) - 1u));
               const int local = 4 * f + c;
-              const float s = scaled(R, penalized_from_global(R, bitmap, local));
+              const float s = scaled(R, penalized_from_global(g, R, bitmap, local));
               if (slot < (uint32_t)kCap) {
-                dsmem_st_f32(dsmem_map(smem_addr(&cand_s[slot]), 0), s);
-                dsmem_st_u32(dsmem_map(smem_addr(&cand_i[slot]), 0), (uint32_t)(R.base + local));
-                dsmem_st_f32(dsmem_map(smem_addr(&cand_e[slot]), 0), t[c]);
+                dsmem_st_f32(dsmem_map(smem_addr(&sm.cand_s[slot]), R.lead), s);
+                dsmem_st_u32(dsmem_map(smem_addr(&sm.cand_i[slot]), R.lead), (uint32_t)(g.base + local));
+                dsmem_st_f32(dsmem_map(smem_addr(&sm.cand_e[slot]), R.lead), t[c]);
               }
               const uint32_t ms = atomicAdd(&ctl.mem_n, 1u);
-              if (ms < (uint32_t)kCap) { mem_s[ms] = s; mem_i[ms] = local; }
+              if (ms < (uint32_t)kCap) { sm.mem_s[ms] = s; sm.mem_i[ms] = local; sm.mem_e[ms] = t[c]; }
             }
           }
         }
       }
+      prefetch();  // the slice is no longer needed
       {
-        const double s = cta_warp_sums(ctl, lane_above, lane, warp, tid);  // ctl.wmass = above masses
-        if (tid == 0) dsmem_st_f64(dsmem_map(smem_addr(&ctl.rec_above[R.rank]), 0), s);
+        const double s = cta_warp_sums(ctl, lane_above, lane, warp);  // ctl.wmass = above masses
+        if (tid == 0) dsmem_st_f64(dsmem_map(smem_addr(&rv.rec_above[g.rank]), R.lead), s);
       }
       cluster_sync();  // barrier: members and above-window masses delivered
       if (leader) {
-        const uint32_t ntot = ctl.cand_n;
+        float* cand_s = sm.cand_s;
+        int32_t* cand_i = sm.cand_i;
+        float* cand_e = sm.cand_e;
+        int32_t* perm = sm.perm;
+        const uint32_t ntot = rv.cand_n;
         const int n = (int)min(ntot, (uint32_t)kCap);
         leader_sort(n, cand_s, cand_i, perm, tid);
         if (warp == 0) {
           double before = 0.0;
-          for (int r = 0; r < kCluster; ++r) before += ctl.rec_above[r];
+          for (int r = 0; r < kCluster; ++r) before += rv.rec_above[r];
           int j0 = -1;
           double run = before;
           if (ntot <= (uint32_t)kCap) {
@@ -1206,9 +1262,9 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
           // kept mass per CTA: above-window mass + kept members (rank order)
           double kept[kCluster];
 #pragma unroll
-          for (int r = 0; r < kCluster; ++r) kept[r] = ctl.rec_above[r];
+          for (int r = 0; r < kCluster; ++r) kept[r] = rv.rec_above[r];
           for (int r = 0; r <= j0 && r < n; ++r) {
-            const int owner_r = cand_i[perm[r]] / R.W;
+            const int owner_r = cand_i[perm[r]] / g.W;
             const double add = (double)cand_e[perm[r]];
 #pragma unroll
             for (int q = 0; q < kCluster; ++q)
@@ -1232,45 +1288,43 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
         }
       }
       cluster_sync();  // barrier: decision delivered
-      const float thr = ctl.bc_thr;
-      const int thr_idx = ctl.bc_thr_idx;
+      K.window = true;
+      K.win_lo = win_lo;
+      K.win_hi = win_hi;
+      K.thr = ctl.bc_thr;
+      K.thr_idx = ctl.bc_thr_idx;
       owner = ctl.bc_owner;
       tloc = ctl.bc_tloc;
       zkept = ctl.bc_z;
-      // drop this CTA's members ranked after the threshold element; add the
-      // kept ones to the per-warp masses (fixed point: order-independent)
+      // add this CTA's kept members to its per-warp masses (fixed point: order-independent)
       if (tid < kWarps) ctl.wfix[tid] = 0ull;
       __syncthreads();
       const int nm = (int)min(ctl.mem_n, (uint32_t)kCap);
       for (int i = tid; i < nm; i += kThreads) {
-        const float sm = mem_s[i];
-        const int li = mem_i[i];
-        if (sm < thr || (sm == thr && R.base + li > thr_idx)) {
-          vals[li] = 0.0f;
-        } else {
-          const int w = min(kWarps - 1, (li >> 2) / R.chunk);
-          atomicAdd(&ctl.wfix[w], (unsigned long long)llrint((double)vals[li] * kFixedScale));
+        const float sm_s = sm.mem_s[i];
+        const int li = sm.mem_i[i];
+        if (!(sm_s < K.thr || (sm_s == K.thr && g.base + li > K.thr_idx))) {
+          const int w = min(kWarps - 1, (li >> 2) / g.chunk);
+          atomicAdd(&ctl.wfix[w], (unsigned long long)llrint((double)sm.mem_e[i] * kFixedScale));
         }
       }
       __syncthreads();
       if (tid < kWarps) ctl.wmass[tid] += (double)ctl.wfix[tid] * kFixedToReal;
       __syncthreads();
-      keep_lo = win_lo;
     }
   }
   if (!topp || !crossed) {
     // plain sampling, large top-k alone, or a top-p that never crosses: draw over all e
-    if (tid < kCluster) dsmem_st_f64(dsmem_map(smem_addr(&ctl.rec_z[R.rank]), tid), ctl.cz[0]);
+    if (tid < kCluster) dsmem_st_f64(dsmem_map(smem_addr(&rv.rec_z[g.rank]), tid), ctl.cz[0]);
     cluster_sync();
-    for (int r = 0; r < kCluster; ++r) zkept += ctl.rec_z[r];
-    pick_owner(ctl.rec_z, u * zkept, owner, tloc);
-    keep_lo = 1u;
+    for (int r = 0; r < kCluster; ++r) zkept += rv.rec_z[r];
+    pick_owner(rv.rec_z, u * zkept, owner, tloc);
   }
 
   // ---- the draw: the owning CTA walks its warps' kept masses in vocabulary order
   if (R.greedy || owner < 0) {
-    if (leader && tid == 0) write_token(a, R.row, gamax);
-  } else if ((int)R.rank == owner) {
+    if (leader && tid == 0) write_token(a.out_tokens, out_i32, row, gamax);
+  } else if ((int)g.rank == owner) {
     int wsel = -1;
     double wpre = 0.0;
     {
@@ -1285,17 +1339,17 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
       if (wsel < 0) { wsel = lastw; wpre = lastpre; }
     }
     if (warp == wsel) {
+      // rows of 32 float4 slots of this warp's piece, recomputed from global memory
+      const int w_begin = wsel * g.chunk, w_end = min(g.nf4, w_begin + g.chunk);
       const double tw = tloc - wpre;
       double run = 0.0;
       int tok = -1, last_kept = -1;
-      for (int f0 = R.f_begin; f0 < R.f_end && tok < 0; f0 += 32) {
+      for (int f0 = w_begin; f0 < w_end && tok < 0; f0 += 32) {
         const int f = f0 + lane;
         float q[4] = {0.f, 0.f, 0.f, 0.f};
-        if (f < R.f_end) {
-          const float4 v = vals4[f];
-          const float t[4] = {v.x, v.y, v.z, v.w};
+        if (f < w_end) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) q[c] = (__float_as_uint(t[c]) >= keep_lo && t[c] > 0.f) ? t[c] : 0.f;
+          for (int c = 0; c < 4; ++c) q[c] = kept_mass(g, R, K, bitmap, 4 * f + c);
         }
         const float ls = __fadd_rn(__fadd_rn(__fadd_rn(q[0], q[1]), q[2]), q[3]);
         const double inc = warp_incl_f64((double)ls, lane);
@@ -1303,7 +1357,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
         int lk = -1;
 #pragma unroll
         for (int c = 0; c < 4; ++c)
-          if (q[c] > 0.f) lk = R.base + 4 * f + c;
+          if (q[c] > 0.f) lk = g.base + 4 * f + c;
         for (int o = 16; o; o >>= 1) lk = max(lk, __shfl_xor_sync(0xffffffffu, lk, o));
         if (lk >= 0) last_kept = lk;
         if (run + rowtot > tw) {
@@ -1321,7 +1375,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
                 }
               }
               if (pick < 0) pick = lastc;
-              tok = R.base + 4 * f + pick;
+              tok = g.base + 4 * f + pick;
             }
             tok = __shfl_sync(0xffffffffu, tok, l);
           }
@@ -1330,21 +1384,90 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
       }
       if (tok < 0) tok = last_kept;
       if (tok < 0) tok = gamax;  // no kept mass at all (cannot happen for a regular row)
-      if (lane == 0) write_token(a, R.row, tok);
+      if (lane == 0) write_token(a.out_tokens, out_i32, row, tok);
     }
   }
   if (debug) {
-    for (int i = tid; i < R.len; i += kThreads) {
-      const float e = vals[i];
-      const bool kept = __float_as_uint(e) >= keep_lo && e > 0.f;
-      if (a.out_probs) a.out_probs[out_off + i] = kept ? (float)((double)e / zkept) : 0.0f;
-      if (a.out_filtered) {
-        float sv = -INFINITY;
-        if (kept) sv = scaled(R, penalized_from_global(R, bitmap, i));
-        a.out_filtered[out_off + i] = sv;
-      }
+    for (int i = tid; i < g.len; i += kThreads) {
+      const float e = kept_mass(g, R, K, bitmap, i);
+      if (a.out_probs) a.out_probs[out_off + i] = e > 0.f ? (float)((double)e / zkept) : 0.0f;
+      if (a.out_filtered)
+        a.out_filtered[out_off + i] = e > 0.f ? scaled(R, penalized_from_global(g, R, bitmap, i)) : -INFINITY;
     }
   }
+}
+
+// ---------------------------------------------------------------- the kernel
+__global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs a, int W, int tma_ok, int vec16_ok) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const Layout L = make_layout(W);
+  Shared sm;
+  sm.ctl = reinterpret_cast<Ctl*>(smem + L.ctl);
+  sm.recv = reinterpret_cast<Recv*>(smem + L.recv);
+  sm.hist = reinterpret_cast<uint32_t*>(smem + L.hist);
+  sm.bitmap = reinterpret_cast<uint32_t*>(smem + L.bitmap);
+  sm.cand_s = reinterpret_cast<float*>(smem + L.cand_s);
+  sm.cand_i = reinterpret_cast<int32_t*>(smem + L.cand_i);
+  sm.cand_e = reinterpret_cast<float*>(smem + L.cand_e);
+  sm.perm = reinterpret_cast<int32_t*>(smem + L.perm);
+  sm.mem_s = reinterpret_cast<float*>(smem + L.mem_s);
+  sm.mem_i = reinterpret_cast<int32_t*>(smem + L.mem_i);
+  sm.mem_e = reinterpret_cast<float*>(smem + L.mem_e);
+  sm.vals = reinterpret_cast<float*>(smem + L.vals);
+  Ctl& ctl = *sm.ctl;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  Src S;
+  S.logits = a.logits;
+  S.sidx = a.sample_indices;
+  S.nrows = a.num_logit_rows;
+  S.stride = a.logits_row_stride;
+  S.bf16 = (a.logits_dtype == NS_DTYPE_BF16);
+  Geo g;
+  g.rank = cluster_ctarank();
+  g.V = a.vocab_size;
+  g.W = W;
+  g.base = (int)g.rank * W;
+  g.len = max(0, min(W, g.V - g.base));
+  g.nf4 = (g.len + 3) >> 2;
+  g.full4 = g.len >> 2;
+  g.chunk = max(1, (g.nf4 + kWarps - 1) / kWarps);
+  g.f_begin = min(g.nf4, warp * g.chunk);
+  g.f_end = min(g.nf4, g.f_begin + g.chunk);
+  g.tma = tma_ok && !S.bf16;
+  g.vec16 = vec16_ok && S.bf16;
+  const int cid = blockIdx.x / kCluster;
+  const int ncl = gridDim.x / kCluster;
+  const int nrows = a.num_rows;
+
+  // one-time setup: barriers and both receive areas
+  if (tid == 0) {
+    for (int w = 0; w < kWarps; ++w) mbar_init(&ctl.mbar[w], 1);
+    fence_mbar_init();
+  }
+  {
+    uint4* r4 = reinterpret_cast<uint4*>(sm.recv);
+    for (int i = tid; i < (int)(2 * sizeof(Recv) / 16); i += kThreads) r4[i] = make_uint4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  cluster_sync();  // every CTA of the cluster runs and is initialised
+  if (cid < nrows) issue_chunk(S, g, ctl, sm.vals, cid, warp, lane);
+
+  uint32_t it = 0;
+  for (int row = cid; row < nrows; row += ncl, ++it) {
+    __syncthreads();  // the previous row is finished in this CTA
+    // clear what peers will write for the next row (they write it only after
+    // this row's first cluster barrier, which waits for this CTA)
+    {
+      uint4* r4 = reinterpret_cast<uint4*>(&sm.recv[(it & 1u) ^ 1u]);
+      for (int i = tid; i < (int)(sizeof(Recv) / 16); i += kThreads) r4[i] = make_uint4(0, 0, 0, 0);
+    }
+    const int next = (row + ncl < nrows) ? row + ncl : -1;
+    bool prefetched = false;
+    process_row(a, S, g, sm, row, next, it & 1u, tid, prefetched);
+    if (!prefetched && next >= 0) issue_chunk(S, g, ctl, sm.vals, next, warp, lane);
+  }
+  cluster_sync();  // nobody leaves while a peer may still address its shared memory
 }
 
 // ---------------------------------------------------------------- host side
@@ -1357,6 +1480,8 @@ int fail(int code, const std::string& msg) {
 
 struct DeviceState {
   size_t smem_set = 0;
+  int max_clusters = 0;
+  size_t clusters_for = 0;
 };
 std::mutex g_mu;
 DeviceState g_dev[64];
@@ -1403,33 +1528,18 @@ int ns_sample(const NsSampleArgs* args, void* stream) {
     return fail(NS_ERR_INVALID_ARG, "ns_sample: fewer logits rows than num_rows and no sample_indices");
   if (a.history_offsets && !a.history_ids)
     return fail(NS_ERR_INVALID_ARG, "ns_sample: history_offsets given without history_ids");
-  if ((int64_t)a.num_rows * kCluster > INT_MAX)
-    return fail(NS_ERR_UNSUPPORTED, "ns_sample: too many rows for one launch");
 
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return fail(NS_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(err));
   const int W = slice_width(a.vocab_size);
   const Layout L = make_layout(W);
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (dev < 0 || dev >= 64) return fail(NS_ERR_UNSUPPORTED, "ns_sample: device ordinal >= 64");
-    if (g_dev[dev].smem_set < L.total) {
-      err = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
-      if (err != cudaSuccess)
-        return fail(NS_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(err));
-      g_dev[dev].smem_set = L.total;
-    }
-  }
-  const uintptr_t p = reinterpret_cast<uintptr_t>(a.logits);
-  const int tma_ok = (a.logits_dtype == NS_DTYPE_F32) && (p % 16 == 0) && (a.logits_row_stride % 4 == 0);
-  const int vec16_ok = (a.logits_dtype == NS_DTYPE_BF16) && (p % 8 == 0) && (a.logits_row_stride % 4 == 0);
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(a.num_rows * kCluster), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = L.total;
-  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = kCluster;
@@ -1437,6 +1547,35 @@ int ns_sample(const NsSampleArgs* args, void* stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+
+  int max_clusters = 0;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (dev < 0 || dev >= 64) return fail(NS_ERR_UNSUPPORTED, "ns_sample: device ordinal >= 64");
+    DeviceState& ds = g_dev[dev];
+    if (ds.smem_set < L.total) {
+      err = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+      if (err != cudaSuccess)
+        return fail(NS_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(err));
+      ds.smem_set = L.total;
+    }
+    if (ds.clusters_for != L.total) {
+      cfg.gridDim = dim3(kCluster, 1, 1);
+      int n = 0;
+      err = cudaOccupancyMaxActiveClusters(&n, sample_kernel, &cfg);
+      if (err != cudaSuccess || n <= 0)
+        return fail(NS_ERR_CUDA, std::string("cudaOccupancyMaxActiveClusters: ") +
+                                     (err != cudaSuccess ? cudaGetErrorString(err) : "no cluster fits"));
+      ds.max_clusters = n;
+      ds.clusters_for = L.total;
+    }
+    max_clusters = ds.max_clusters;
+  }
+  const int clusters = a.num_rows < max_clusters ? a.num_rows : max_clusters;
+  cfg.gridDim = dim3((unsigned)(clusters * kCluster), 1, 1);
+  const uintptr_t p = reinterpret_cast<uintptr_t>(a.logits);
+  const int tma_ok = (a.logits_dtype == NS_DTYPE_F32) && (p % 16 == 0) && (a.logits_row_stride % 4 == 0);
+  const int vec16_ok = (a.logits_dtype == NS_DTYPE_BF16) && (p % 8 == 0) && (a.logits_row_stride % 4 == 0);
   err = cudaLaunchKernelEx(&cfg, sample_kernel, a, W, tma_ok, vec16_ok);
   if (err != cudaSuccess) return fail(NS_ERR_CUDA, std::string("sample kernel launch: ") + cudaGetErrorString(err));
   return NS_OK;
