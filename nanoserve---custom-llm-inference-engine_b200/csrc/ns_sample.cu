@@ -9,13 +9,14 @@
 //    it, so every row crosses HBM exactly once.  Each warp moves its own
 //    contiguous piece of the slice with one mbarrier-tracked bulk copy
 //    (cp.async.bulk, global -> own shared memory, no multicast) and issues
-//    the copy for the NEXT row as soon as it has finished reading the
-//    current one, so HBM keeps streaming while the cluster exchanges
-//    statistics, waits at barriers and decides.
+//    the copy for the NEXT row as soon as it has finished with the current
+//    one, so HBM keeps streaming while the cluster exchanges statistics,
+//    waits at barriers and decides.  The next row's parameters are fetched
+//    with cp.async during the current row.
 //  * Row statistics, histograms and candidate lists are exchanged through
 //    distributed shared memory (st/ld/red/atom .shared::cluster) between
 //    cluster barriers.  Areas that peers write into are double-buffered by
-//    row parity.  No global scratch memory is used.
+//    row parity; the row's leader CTA rotates.  No global scratch memory.
 //  * Three row paths, chosen per row (uniformly across the cluster):
 //      GREEDY   temperature == 0 and no debug output: first-index argmax
 //               (sampler.py:82-83); one exchange.
@@ -30,10 +31,10 @@
 //               (log-spaced buckets, one 32-bit shared atomic per element),
 //               narrows it to a window of buckets that must contain the
 //               boundary, then ships the window's elements to the leader,
-//               which ranks them and decides exactly with the exact mass
+//               which sorts them and decides exactly with the exact mass
 //               above the window.  Large top-k runs an exact 3-level radix
 //               select first.  The draw walks per-warp masses in vocabulary
-//               order.
+//               order, then one warp's piece of the slice.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -57,7 +58,7 @@ constexpr int kCoarse = 64;          // coarse buckets of kFine fine buckets
 constexpr int kFine = kBins / kCoarse;
 constexpr int kRadixBins = 2048;     // radix-select level histogram (u32 counts), 2 buffers
 constexpr int kRadixCoarse = 32;
-constexpr int kCap = 512;            // leader candidate list capacity
+constexpr int kCap = 512;            // leader candidate list capacity (a power of two)
 constexpr int kTopkSmall = 128;      // largest top_k served by the TOPK path
 constexpr int kTmBins = 2048;        // per-thread-maximum histogram (u16 counts), quarter binades
 constexpr int kTmShift = 21;
@@ -69,10 +70,10 @@ constexpr double kFixedScale = 17592186044416.0;  // 2^44
 
 // What peers write into this CTA during one row; double-buffered by row parity.
 struct __align__(16) Recv {
-  float rec_max[kCluster];
-  float rec_min[kCluster];
-  float rec_amin[kCluster];
-  int32_t rec_amax[kCluster];
+  uint32_t rec_kmax[kCluster];   // orderable key of the CTA maximum (0xffffffff: NaN seen)
+  uint32_t rec_kmin[kCluster];   // orderable key of the CTA minimum
+  float rec_amin[kCluster];      // smallest |x|
+  int32_t rec_amax[kCluster];    // first index of the CTA maximum
   int32_t rec_nan[kCluster];
   int32_t rec_pinf[kCluster];
   double rec_z[kCluster];
@@ -83,9 +84,18 @@ struct __align__(16) Recv {
   uint32_t tm_global[kTmBins / 2];
 };
 
+// One row's inputs, fetched one row ahead.
+struct __align__(16) RowIn {
+  NsRowParams P;
+  int64_t h[2];
+  int64_t src;
+  int64_t pad;
+};
+
 // Fixed-size control block at the start of dynamic shared memory.
 struct __align__(16) Ctl {
   uint64_t mbar[kWarps];
+  RowIn rin[2];
   // own coarse sums, double-buffered by level (peers read them)
   double cmass[2][kCoarse];
   uint32_t ccnt[2][kRadixCoarse];
@@ -106,21 +116,22 @@ struct __align__(16) Ctl {
   float sel_est;
   double sel_z;
   // reductions
-  float red_a[kWarps];
-  float red_b[kWarps];
-  float red_c[kWarps];
+  uint32_t red_k[kWarps];
+  uint32_t red_m[kWarps];
+  uint32_t red_a[kWarps];
   int32_t red_i[kWarps];
   int32_t red_j[kWarps];
   uint32_t red_u[kWarps];
   double wmass[kWarps];
   unsigned long long wfix[kWarps];
   int32_t misc_i;
+  int32_t misc_j;
   int32_t token;
   uint32_t mem_n;
 };
 
 struct Layout {
-  size_t ctl, recv, hist, bitmap, cand_s, cand_i, cand_e, perm, mem_s, mem_i, mem_e, vals, total;
+  size_t ctl, recv, hist, bitmap, cand_s, cand_i, keys, mem_s, mem_i, mem_e, vals, total;
 };
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
@@ -134,8 +145,7 @@ __host__ __device__ inline Layout make_layout(int W) {
   L.bitmap = o; o = align16(o + sizeof(uint32_t) * ((W + 31) / 32));
   L.cand_s = o; o = align16(o + sizeof(float) * kCap);
   L.cand_i = o; o = align16(o + sizeof(int32_t) * kCap);
-  L.cand_e = o; o = align16(o + sizeof(float) * kCap);
-  L.perm = o;   o = align16(o + sizeof(int32_t) * kCap);
+  L.keys = o;   o = align16(o + sizeof(unsigned long long) * kCap);
   L.mem_s = o;  o = align16(o + sizeof(float) * kCap);
   L.mem_i = o;  o = align16(o + sizeof(int32_t) * kCap);
   L.mem_e = o;  o = align16(o + sizeof(float) * kCap);
@@ -145,29 +155,10 @@ __host__ __device__ inline Layout make_layout(int W) {
 }
 
 // ---------------------------------------------------------------- warp helpers
-__device__ __forceinline__ float warp_min(float v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-__device__ __forceinline__ int warp_imin(int v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
 __device__ __forceinline__ double warp_dsum(double v) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
-}
-// (value, index) argmax with first-index tie break; NaN values are ignored
-__device__ __forceinline__ void warp_argmax(float& v, int& i) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) {
-    float ov = __shfl_xor_sync(0xffffffffu, v, o);
-    int oi = __shfl_xor_sync(0xffffffffu, i, o);
-    if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
-  }
 }
 __device__ __forceinline__ uint32_t warp_incl_u32(uint32_t v, int lane) {
 #pragma unroll
@@ -191,6 +182,35 @@ __device__ __forceinline__ double warp_incl_f64(double v, int lane) {
 // inclusive mass passes this test is the last one kept.
 __device__ __forceinline__ bool topp_crossed(double cum, double z, float p) {
   return (float)(cum / z) > p;
+}
+
+// Sort key: ascending keys give (value descending, index ascending).
+__device__ __forceinline__ unsigned long long rank_key(float s, int idx) {
+  return ((unsigned long long)(~f2key(s)) << 32) | (uint32_t)idx;
+}
+__device__ __forceinline__ float key_value(unsigned long long k) { return key2f(~(uint32_t)(k >> 32)); }
+__device__ __forceinline__ int key_index(unsigned long long k) { return (int)(uint32_t)k; }
+
+// Bitonic sort of keys[0, n) ascending in place (n <= kCap), by the whole CTA.
+// Entries [n, pow2) are filled with the largest key.
+__device__ void bitonic_sort(unsigned long long* keys, int n, int tid) {
+  int np = 1;
+  while (np < n) np <<= 1;
+  for (int i = n + tid; i < np; i += kThreads) keys[i] = ~0ull;
+  __syncthreads();
+  for (int k = 2; k <= np; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < np; i += kThreads) {
+        const int l = i ^ j;
+        if (l > i) {
+          const unsigned long long a = keys[i], b = keys[l];
+          const bool up = (i & k) == 0;
+          if ((a > b) == up) { keys[i] = b; keys[l] = a; }
+        }
+      }
+      __syncthreads();
+    }
+  }
 }
 
 // ---------------------------------------------------------------- contexts
@@ -296,10 +316,12 @@ __device__ __forceinline__ float4 load_slot(const Geo& g, const Row& R, float* v
   return v;
 }
 
-// Issue this warp's bulk copy of row `row` into its piece of the slice.
-// The warp must be done reading and writing that piece for the current row.
+// Issue this warp's bulk copy of row `row` into its piece of the slice.  The
+// warp must be done reading and writing that piece for the current row.
+// Every lane orders its own earlier shared-memory writes before the copy.
 __device__ __forceinline__ void issue_chunk(const Src& S, const Geo& g, Ctl& ctl, float* vals, int row, int warp,
                                             int lane) {
+  fence_proxy_async_smem();
   __syncwarp();
   if (!g.tma || lane != 0) return;
   const int fe = min(g.f_end, g.full4);
@@ -308,7 +330,6 @@ __device__ __forceinline__ void issue_chunk(const Src& S, const Geo& g, Ctl& ctl
   const int64_t src = source_row(S, row, bad);
   const float* p = reinterpret_cast<const float*>(S.logits) + src * S.stride + g.base + 4 * g.f_begin;
   const uint32_t bytes = (uint32_t)(fe - g.f_begin) * 16u;
-  fence_proxy_async_smem();
   mbar_arrive_expect_tx(&ctl.mbar[warp], bytes);
   bulk_g2s(vals + 4 * g.f_begin, p, bytes, &ctl.mbar[warp]);
 }
@@ -324,8 +345,29 @@ __device__ __forceinline__ void wait_chunk(const Geo& g, Ctl& ctl, int warp, uin
       if (status) atomicOr(status, NS_STATUS_WAIT_TIMEOUT);
       break;
     }
-    if (spins > 64) __nanosleep(128);
+    if (spins > 64) __nanosleep(64);
   }
+}
+
+// Threads 0..3 start fetching row `row`'s inputs into `dst` (cp.async).
+__device__ __forceinline__ void fetch_row_inputs(const NsSampleArgs& a, RowIn& dst, int row, int tid) {
+  if (tid == 0) {
+    cp_async16(&dst.P, &a.row_params[row]);
+  } else if (tid == 1) {
+    cp_async16(reinterpret_cast<char*>(&dst.P) + 16, reinterpret_cast<const char*>(&a.row_params[row]) + 16);
+  } else if (tid == 2) {
+    if (a.history_offsets) {
+      cp_async8(&dst.h[0], &a.history_offsets[row]);
+      cp_async8(&dst.h[1], &a.history_offsets[row + 1]);
+    } else {
+      dst.h[0] = 0;
+      dst.h[1] = 0;
+    }
+  } else if (tid == 3) {
+    if (a.sample_indices) cp_async8(&dst.src, &a.sample_indices[row]);
+    else dst.src = row;
+  }
+  if (tid < 4) cp_async_commit();
 }
 
 // Smallest float c <= b with RN(c/T) == RN(b/T): the lower end of the set of
@@ -542,22 +584,6 @@ __device__ void topp_window(Ctl& ctl, const uint32_t* h, int buf, const Level& l
   __syncthreads();
 }
 
-// Rank-by-counting of the leader's n candidates: perm[rank] = i with order
-// (s descending, index ascending).  n <= kCap.
-__device__ void leader_sort(int n, const float* cs, const int32_t* ci, int32_t* perm, int tid) {
-  for (int i = tid; i < n; i += kThreads) {
-    const float si = cs[i];
-    const int ii = ci[i];
-    int r = 0;
-    for (int j = 0; j < n; ++j) {
-      const float sj = cs[j];
-      r += (sj > si) || (sj == si && ci[j] < ii);
-    }
-    perm[r] = i;
-  }
-  __syncthreads();
-}
-
 // Per-warp sums of lane values (into ctl.wmass) and their CTA total.
 __device__ __forceinline__ double cta_warp_sums(Ctl& ctl, float lane_v, int lane, int warp) {
   const double w = warp_dsum((double)lane_v);
@@ -581,8 +607,21 @@ __device__ __forceinline__ void pick_owner(const double* m, double target, int& 
   }
   if (owner < 0) { owner = last; tloc = target - last_pre; }
 }
+// First warp whose mass prefix passes target, and the target within it.
+__device__ __forceinline__ void pick_warp(const double* m, double target, int& w, double& tw) {
+  double run = 0.0, lastpre = 0.0;
+  int lastw = -1;
+  w = -1;
+  for (int i = 0; i < kWarps; ++i) {
+    const double x = m[i];
+    if (x > 0.0) { lastw = i; lastpre = run; }
+    if (w < 0 && x > 0.0 && run + x > target) { w = i; tw = target - run; }
+    run += x;
+  }
+  if (w < 0) { w = lastw; tw = target - lastpre; }
+}
 
-// What the owner warp needs to recompute kept masses from global memory.
+// What the debug outputs need to recompute kept masses from global memory.
 struct Keep {
   float m;             // max scaled logit
   bool have_thr_k;     // large top-k mask: s >= thr_k_s
@@ -607,6 +646,59 @@ __device__ __forceinline__ float kept_mass(const Geo& g, const Row& R, const Kee
   return e;
 }
 
+// The selected warp walks its piece of the slice (masses e in shared memory,
+// kept <=> bits(e) >= keep_lo and e > 0) in vocabulary order until the mass
+// passes tw; returns the token (lane-uniform).
+__device__ int walk_warp(const Geo& g, const float4* vals4, int wsel, uint32_t keep_lo, double tw, int lane,
+                         int fallback) {
+  const int w_begin = min(g.nf4, wsel * g.chunk), w_end = min(g.nf4, w_begin + g.chunk);
+  double run = 0.0;
+  int tok = -1, last_kept = -1;
+  for (int f0 = w_begin; f0 < w_end && tok < 0; f0 += 32) {
+    const int f = f0 + lane;
+    float q[4] = {0.f, 0.f, 0.f, 0.f};
+    if (f < w_end) {
+      const float4 v = vals4[f];
+      const float t[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) q[c] = (__float_as_uint(t[c]) >= keep_lo && t[c] > 0.f) ? t[c] : 0.f;
+    }
+    const float ls = __fadd_rn(__fadd_rn(__fadd_rn(q[0], q[1]), q[2]), q[3]);
+    const double inc = warp_incl_f64((double)ls, lane);
+    const double rowtot = __shfl_sync(0xffffffffu, inc, 31);
+    int lk = -1;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      if (q[c] > 0.f) lk = g.base + 4 * f + c;
+    lk = __reduce_max_sync(0xffffffffu, (uint32_t)(lk + 1)) - 1;
+    if (lk >= 0) last_kept = lk;
+    if (run + rowtot > tw) {
+      const uint32_t bal = __ballot_sync(0xffffffffu, run + inc > tw && ls > 0.f);
+      if (bal) {
+        const int l = __ffs(bal) - 1;
+        if (lane == l) {
+          double cum = run + inc - (double)ls;
+          int pick = -1, lastc = -1;
+          for (int c = 0; c < 4; ++c) {
+            if (q[c] > 0.f) {
+              lastc = c;
+              cum += (double)q[c];
+              if (pick < 0 && cum > tw) pick = c;
+            }
+          }
+          if (pick < 0) pick = lastc;
+          tok = g.base + 4 * f + pick;
+        }
+        tok = __shfl_sync(0xffffffffu, tok, l);
+      }
+    }
+    run += rowtot;
+  }
+  if (tok < 0) tok = last_kept;
+  if (tok < 0) tok = fallback;
+  return tok;
+}
+
 // ---------------------------------------------------------------- one row
 struct Shared {
   Ctl* ctl;
@@ -615,19 +707,20 @@ struct Shared {
   uint32_t* bitmap;
   float* cand_s;
   int32_t* cand_i;
-  float* cand_e;
-  int32_t* perm;
+  unsigned long long* keys;
   float* mem_s;
   int32_t* mem_i;
   float* mem_e;
   float* vals;
 };
 
-// Samples `row`.  Every path issues this warp's bulk copy of `next_row` as
-// soon as the warp has finished with its piece of the slice and records that
-// in `prefetched`; the caller issues it at the end of the row otherwise.
+// Samples `row` (its inputs are in ctl.rin[par]).  Every path issues this
+// warp's bulk copy of `next_row` as soon as the warp has finished with its
+// piece of the slice and records that in `prefetched`; the caller issues it
+// at the end of the row otherwise.
 __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S, const Geo& g, const Shared& sm,
-                                            int row, int next_row, uint32_t par, int tid, bool& prefetched) {
+                                            int row, int next_row, uint32_t par, uint32_t lead, int tid,
+                                            bool& prefetched) {
   const int lane = tid & 31, warp = tid >> 5;
   Ctl& ctl = *sm.ctl;
   Recv& rv = sm.recv[par];
@@ -644,12 +737,14 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
     }
   };
 
+  const RowIn& in = ctl.rin[par];
   Row R;
   R.row = row;
-  R.lead = (uint32_t)(row & (kCluster - 1));
-  const bool leader = (g.rank == R.lead);
-  bool bad_row;
-  const int64_t src = source_row(S, row, bad_row);
+  R.lead = lead;
+  const bool leader = (g.rank == lead);
+  int64_t src = in.src;
+  const bool bad_row = (src < 0 || src >= S.nrows);
+  if (bad_row) src = 0;
   if (S.bf16) {
     R.src16 = reinterpret_cast<const __nv_bfloat16*>(S.logits) + src * S.stride;
     R.src32 = nullptr;
@@ -657,7 +752,7 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
     R.src32 = reinterpret_cast<const float*>(S.logits) + src * S.stride;
     R.src16 = nullptr;
   }
-  const NsRowParams P = a.row_params[row];
+  const NsRowParams P = in.P;
   R.greedy = (P.flags & NS_ROW_GREEDY) != 0u;
   R.T = R.greedy ? 1.0f : P.temperature;
   R.rT = __frcp_rn(R.T);
@@ -666,12 +761,8 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
   R.p = P.top_p;
   R.k = (P.top_k > 0 && P.top_k < g.V) ? P.top_k : 0;
   R.rp = P.repetition_penalty;
-  int64_t h0 = 0, h1 = 0;
-  if (a.history_offsets && (P.flags & NS_ROW_PENALTY)) {
-    h0 = a.history_offsets[row];
-    h1 = a.history_offsets[row + 1];
-  }
-  R.pen = (P.flags & NS_ROW_PENALTY) != 0u && h1 > h0;
+  const int64_t h0 = in.h[0], h1 = in.h[1];
+  R.pen = (P.flags & NS_ROW_PENALTY) != 0u && a.history_offsets && h1 > h0;
   const bool debug = (a.out_filtered != nullptr) || (a.out_probs != nullptr);
   const int64_t out_off = (int64_t)row * g.V + g.base;
   float* pen_out = a.out_penalized ? a.out_penalized + out_off : nullptr;
@@ -682,7 +773,8 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
 
   // ---------------- per-row setup (the caller synchronised the CTA)
   if (tid == 0) ctl.mem_n = 0u;
-  for (int i = tid; i < kBins / 4; i += kThreads) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
+  if (mode0 == kTopk)
+    for (int i = tid; i < kTmBins / 8; i += kThreads) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
   if (R.pen) {
     for (int i = tid; i < (g.W + 31) / 32; i += kThreads) bitmap[i] = 0u;
     __syncthreads();
@@ -741,39 +833,36 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
     const uint32_t b = f2key(st_max) >> kTmShift;
     atomicAdd(&hist[b >> 1], 1u << ((b & 1u) << 4));
   }
-  // CTA reduction of (max with NaN propagation, argmax, min, min |x|)
+  // CTA reduction: (max with NaN seen, first argmax, min, min |x|) via redux
   {
     const bool lane_nan = (st_max != st_max);
-    const bool warp_nan = __any_sync(0xffffffffu, lane_nan);
-    float vmax = lane_nan ? -INFINITY : st_max;
-    int vi = st_amax;
-    warp_argmax(vmax, vi);
-    const float vmin = warp_min(st_min);
-    const float vamin = warp_min(st_amin);
+    const uint32_t kmax = lane_nan ? 0u : f2key(st_max);
+    const uint32_t wk = __reduce_max_sync(0xffffffffu, kmax);
+    const int wi = (int)__reduce_min_sync(0xffffffffu, (kmax == wk) ? (uint32_t)st_amax : 0x7fffffffu);
+    const bool wnan = __any_sync(0xffffffffu, lane_nan);
+    const uint32_t wmin = __reduce_min_sync(0xffffffffu, f2key(st_min));
+    const uint32_t wamin = __reduce_min_sync(0xffffffffu, __float_as_uint(st_amin));
     if (lane == 0) {
-      ctl.red_a[warp] = warp_nan ? __int_as_float(0x7fc00000) : vmax;
-      ctl.red_i[warp] = vi;
-      ctl.red_b[warp] = vmin;
-      ctl.red_c[warp] = vamin;
+      ctl.red_k[warp] = wnan ? 0xffffffffu : wk;
+      ctl.red_i[warp] = wi;
+      ctl.red_m[warp] = wmin;
+      ctl.red_a[warp] = wamin;
     }
     __syncthreads();
-    if (tid < kCluster) {
-      float m = -INFINITY, mn = INFINITY, amn = INFINITY;
-      int mi = INT_MAX;
-      bool nan_any = false;
-      for (int w = 0; w < kWarps; ++w) {
-        const float x = ctl.red_a[w];
-        const int xi = ctl.red_i[w];
-        if (x != x) nan_any = true;
-        else if (x > m || (x == m && xi < mi)) { m = x; mi = xi; }
-        mn = fminf(mn, ctl.red_b[w]);
-        amn = fminf(amn, ctl.red_c[w]);
+    if (warp == 0) {
+      const bool live = lane < kWarps;
+      const uint32_t k = live ? ctl.red_k[lane] : 0u;
+      const uint32_t ck = __reduce_max_sync(0xffffffffu, k);
+      const int ci = (int)__reduce_min_sync(0xffffffffu, (live && k == ck) ? (uint32_t)ctl.red_i[lane] : 0x7fffffffu);
+      const uint32_t cm = __reduce_min_sync(0xffffffffu, live ? ctl.red_m[lane] : 0xffffffffu);
+      const uint32_t ca = __reduce_min_sync(0xffffffffu, live ? ctl.red_a[lane] : 0x7f800000u);
+      if (lane < kCluster) {
+        const uint32_t r = (uint32_t)lane;
+        dsmem_st_u32(dsmem_map(smem_addr(&rv.rec_kmax[g.rank]), r), ck);
+        dsmem_st_u32(dsmem_map(smem_addr(&rv.rec_kmin[g.rank]), r), cm);
+        dsmem_st_u32(dsmem_map(smem_addr(&rv.rec_amin[g.rank]), r), ca);
+        dsmem_st_u32(dsmem_map(smem_addr(&rv.rec_amax[g.rank]), r), (uint32_t)ci);
       }
-      const uint32_t r = (uint32_t)tid;
-      dsmem_st_f32(dsmem_map(smem_addr(&rv.rec_max[g.rank]), r), nan_any ? __int_as_float(0x7fc00000) : m);
-      dsmem_st_f32(dsmem_map(smem_addr(&rv.rec_min[g.rank]), r), mn);
-      dsmem_st_f32(dsmem_map(smem_addr(&rv.rec_amin[g.rank]), r), amn);
-      dsmem_st_u32(dsmem_map(smem_addr(&rv.rec_amax[g.rank]), r), (uint32_t)mi);
     }
   }
   if (mode0 == kTopk) {
@@ -788,16 +877,18 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
   }
   cluster_sync();  // barrier 1: records (and maxima histograms) delivered
 
-  float gmax = -INFINITY, gmin = INFINITY, gamin = INFINITY;
+  uint32_t gk = 0u, gkmin = 0xffffffffu;
+  float gamin = INFINITY;
   int gamax = INT_MAX;
-  bool gnan = false;
   for (int r = 0; r < kCluster; ++r) {
-    const float x = rv.rec_max[r];
-    if (x != x) gnan = true;
-    else if (x > gmax) { gmax = x; gamax = rv.rec_amax[r]; }
-    gmin = fminf(gmin, rv.rec_min[r]);
+    const uint32_t k = rv.rec_kmax[r];
+    if (k > gk) { gk = k; gamax = rv.rec_amax[r]; }
+    gkmin = min(gkmin, rv.rec_kmin[r]);
     gamin = fminf(gamin, rv.rec_amin[r]);
   }
+  const bool gnan = (gk == 0xffffffffu);
+  const float gmax = gnan ? __int_as_float(0x7fc00000) : key2f(gk);
+  const float gmin = key2f(gkmin);
   if (gmax == -INFINITY) gamax = 0;
 
   // ---------------- rows whose softmax is NaN: uniform 1/V (sampler.py:76-80)
@@ -813,8 +904,8 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
         if (x != x) my_nan = min(my_nan, g.base + i);
         if (x == INFINITY) my_pinf = min(my_pinf, g.base + i);
       }
-      my_nan = warp_imin(my_nan);
-      my_pinf = warp_imin(my_pinf);
+      my_nan = (int)__reduce_min_sync(0xffffffffu, (uint32_t)my_nan);
+      my_pinf = (int)__reduce_min_sync(0xffffffffu, (uint32_t)my_pinf);
       if (lane == 0) { ctl.red_i[warp] = my_nan; ctl.red_j[warp] = my_pinf; }
       __syncthreads();
       if (tid < kCluster) {
@@ -847,7 +938,7 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
     return;
   }
 
-  const uint32_t cand_n_lead = dsmem_map(smem_addr(&rv.cand_n), R.lead);
+  const uint32_t cand_n_lead = dsmem_map(smem_addr(&rv.cand_n), lead);
   bool need_min = false;
 
   // ================================================================ TOPK
@@ -898,8 +989,8 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
           if (take) {
             const uint32_t slot = slot0 + (uint32_t)__popc(bal & ((1u << lane) - 1u));
             if (slot < (uint32_t)kCap) {
-              dsmem_st_f32(dsmem_map(smem_addr(&sm.cand_s[slot]), R.lead), scaled(R, t[c]));
-              dsmem_st_u32(dsmem_map(smem_addr(&sm.cand_i[slot]), R.lead), (uint32_t)(g.base + 4 * f + c));
+              dsmem_st_f32(dsmem_map(smem_addr(&sm.cand_s[slot]), lead), scaled(R, t[c]));
+              dsmem_st_u32(dsmem_map(smem_addr(&sm.cand_i[slot]), lead), (uint32_t)(g.base + 4 * f + c));
             } else if (slot == (uint32_t)kCap) {
               for (int r = 0; r < kCluster; ++r) dsmem_st_u32(dsmem_map(smem_addr(&rv.overflow), r), 1u);
             }
@@ -914,34 +1005,41 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
         const int n = (int)rv.cand_n;
         float* cand_s = sm.cand_s;
         int32_t* cand_i = sm.cand_i;
-        float* cand_e = sm.cand_e;
-        int32_t* perm = sm.perm;
+        unsigned long long* keys = sm.keys;
         if (n == 0) {  // impossible while the bound holds; keep the kernel total anyway
           if (tid == 0) write_token(a.out_tokens, out_i32, row, gamax);
         } else {
-          leader_sort(n, cand_s, cand_i, perm, tid);
-          const float s0 = cand_s[perm[0]];
-          const int kk = min(R.k, n);
-          const float thr = cand_s[perm[kk - 1]];
+          // candidates in rank order (value desc, index asc)
+          for (int i = tid; i < n; i += kThreads) keys[i] = rank_key(cand_s[i], cand_i[i]);
+          bitonic_sort(keys, n, tid);
+          for (int r = tid; r < n; r += kThreads) {
+            cand_s[r] = key_value(keys[r]);
+            cand_i[r] = key_index(keys[r]);
+          }
+          __syncthreads();
+          const float s0 = cand_s[0];
+          const float thr = cand_s[min(R.k, n) - 1];
           if (tid == 0) { ctl.misc_i = n; ctl.token = INT_MAX; }
           __syncthreads();
           for (int r = tid; r < n; r += kThreads) {
-            const bool in = cand_s[perm[r]] >= thr;
-            const bool nxt = (r + 1 < n) && (cand_s[perm[r + 1]] >= thr);
-            if (in && !nxt) ctl.misc_i = r + 1;
+            const bool in1 = cand_s[r] >= thr;
+            const bool nxt = (r + 1 < n) && (cand_s[r + 1] >= thr);
+            if (in1 && !nxt) ctl.misc_i = r + 1;
           }
           __syncthreads();
           const int n1 = ctl.misc_i;  // survivors of top-k (ties at the threshold kept)
-          for (int r = tid; r < n1; r += kThreads) cand_e[r] = exp_shifted(cand_s[perm[r]], s0);
+          float* cand_e = sm.mem_e;   // masses by rank (the member list is unused on this path)
+          for (int r = tid; r < n1; r += kThreads) cand_e[r] = exp_shifted(cand_s[r], s0);
           __syncthreads();
           int n2 = n1;
-          if (R.topp) {
-            if (warp == 0) {
-              double z = 0.0;
-              for (int c0 = 0; c0 < n1; c0 += 32) {
-                const int r = c0 + lane;
-                z += warp_dsum(r < n1 ? (double)cand_e[r] : 0.0);
-              }
+          if (warp == 0) {
+            double z = 0.0;
+            for (int c0 = 0; c0 < n1; c0 += 32) {
+              const int r = c0 + lane;
+              z += warp_dsum(r < n1 ? (double)cand_e[r] : 0.0);
+            }
+            int m2 = n1;
+            if (R.topp) {
               double run = 0.0;
               int j0 = -1;
               for (int c0 = 0; c0 < n1 && j0 < 0; c0 += 32) {
@@ -952,29 +1050,26 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
                 run = __shfl_sync(0xffffffffu, inc, 31);
               }
               // keep exactly ranks 0..j0 in (value desc, index asc) order
-              if (lane == 0) ctl.misc_i = (j0 >= 0) ? j0 + 1 : n1;
+              if (j0 >= 0) m2 = j0 + 1;
+              z = 0.0;
+              for (int c0 = 0; c0 < m2; c0 += 32) {
+                const int r = c0 + lane;
+                z += warp_dsum(r < m2 ? (double)cand_e[r] : 0.0);
+              }
             }
-            __syncthreads();
-            n2 = ctl.misc_i;
-          }
-          // total kept mass (rank order) and the inverse-CDF draw in vocabulary order
-          if (warp == 0) {
-            double z = 0.0;
-            for (int c0 = 0; c0 < n2; c0 += 32) {
-              const int r = c0 + lane;
-              z += warp_dsum(r < n2 ? (double)cand_e[r] : 0.0);
-            }
-            if (lane == 0) ctl.sel_z = z;
+            if (lane == 0) { ctl.misc_i = m2; ctl.sel_z = z; }
           }
           __syncthreads();
+          n2 = ctl.misc_i;
           const double z2 = ctl.sel_z;
           const double target = u * z2;
+          // inverse CDF in vocabulary order over the kept ranks
           for (int r = tid; r < n2; r += kThreads) {
-            const int ir = cand_i[perm[r]];
+            const int ir = cand_i[r];
             const double er = (double)cand_e[r];
             double before = 0.0;
             for (int q = 0; q < n2; ++q)
-              if (cand_i[perm[q]] < ir) before += (double)cand_e[q];
+              if (cand_i[q] < ir) before += (double)cand_e[q];
             if (er > 0.0 && before <= target && target < before + er) atomicMin(&ctl.token, ir);
           }
           __syncthreads();
@@ -984,17 +1079,15 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
               // target at the very top (rounding): the last kept element with mass
               int last = -1;
               for (int r = 0; r < n2; ++r)
-                if (cand_e[r] > 0.f && cand_i[perm[r]] > last) last = cand_i[perm[r]];
-              tok = last >= 0 ? last : cand_i[perm[0]];
+                if (cand_e[r] > 0.f && cand_i[r] > last) last = cand_i[r];
+              tok = last >= 0 ? last : cand_i[0];
             }
-            if (R.greedy) tok = cand_i[perm[0]];
+            if (R.greedy) tok = cand_i[0];
             write_token(a.out_tokens, out_i32, row, tok);
             if (debug) {
-              const float thr2 = cand_s[perm[n2 - 1]];
-              const int thr_idx = cand_i[perm[n2 - 1]];
               for (int r = 0; r < kCluster; ++r) {
-                dsmem_st_f32(dsmem_map(smem_addr(&ctl.bc_thr), r), thr2);
-                dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_thr_idx), r), (uint32_t)thr_idx);
+                dsmem_st_f32(dsmem_map(smem_addr(&ctl.bc_thr), r), cand_s[n2 - 1]);
+                dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_thr_idx), r), (uint32_t)cand_i[n2 - 1]);
                 dsmem_st_f32(dsmem_map(smem_addr(&ctl.bc_m), r), s0);
                 dsmem_st_f64(dsmem_map(smem_addr(&ctl.bc_z), r), z2);
               }
@@ -1022,6 +1115,7 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
   }
 
   // ================================================================ GENERAL
+  float gmin2 = gmin, gamin2 = gamin;
   if (need_min) {
     // statistics the TOPK pass did not gather: min and min |x|
     float mn = INFINITY, amn = INFINITY;
@@ -1030,25 +1124,26 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
       mn = fminf(mn, fminf(fminf(v.x, v.y), fminf(v.z, v.w)));
       amn = fminf(amn, fminf(fminf(fabsf(v.x), fabsf(v.y)), fminf(fabsf(v.z), fabsf(v.w))));
     }
-    mn = warp_min(mn);
-    amn = warp_min(amn);
-    if (lane == 0) { ctl.red_b[warp] = mn; ctl.red_c[warp] = amn; }
+    const uint32_t wm = __reduce_min_sync(0xffffffffu, f2key(mn));
+    const uint32_t wa = __reduce_min_sync(0xffffffffu, __float_as_uint(amn));
+    if (lane == 0) { ctl.red_m[warp] = wm; ctl.red_a[warp] = wa; }
     __syncthreads();
     if (tid < kCluster) {
-      float m2 = INFINITY, a2 = INFINITY;
-      for (int w = 0; w < kWarps; ++w) { m2 = fminf(m2, ctl.red_b[w]); a2 = fminf(a2, ctl.red_c[w]); }
-      dsmem_st_f32(dsmem_map(smem_addr(&rv.rec_min[g.rank]), tid), m2);
-      dsmem_st_f32(dsmem_map(smem_addr(&rv.rec_amin[g.rank]), tid), a2);
+      uint32_t m2 = 0xffffffffu, a2 = 0x7f800000u;
+      for (int w = 0; w < kWarps; ++w) { m2 = min(m2, ctl.red_m[w]); a2 = min(a2, ctl.red_a[w]); }
+      dsmem_st_u32(dsmem_map(smem_addr(&rv.rec_kmin[g.rank]), tid), m2);
+      dsmem_st_u32(dsmem_map(smem_addr(&rv.rec_amin[g.rank]), tid), a2);
     }
     if (leader && tid == 0) rv.cand_n = 0u;
     cluster_sync();
-    gmin = INFINITY;
-    gamin = INFINITY;
-    for (int r = 0; r < kCluster; ++r) { gmin = fminf(gmin, rv.rec_min[r]); gamin = fminf(gamin, rv.rec_amin[r]); }
+    uint32_t km = 0xffffffffu;
+    gamin2 = INFINITY;
+    for (int r = 0; r < kCluster; ++r) { km = min(km, rv.rec_kmin[r]); gamin2 = fminf(gamin2, rv.rec_amin[r]); }
+    gmin2 = key2f(km);
   }
   // The guard-free division needs every |x| of the row in [2^-40, 2^80] and T <= 2^20.
-  const float gabsmax = fmaxf(fabsf(gmax), fabsf(gmin));
-  const bool fast_div = !R.t_one && gamin >= 0x1p-40f && gabsmax <= 0x1p+80f && R.T <= 0x1p+20f;
+  const float gabsmax = fmaxf(fabsf(gmax), fabsf(gmin2));
+  const bool fast_div = !R.t_one && gamin2 >= 0x1p-40f && gabsmax <= 0x1p+80f && R.T <= 0x1p+20f;
   Keep K;
   K.m = R.t_one ? gmax : __fdiv_rn(gmax, R.T);  // max scaled logit (division is monotone)
   K.have_thr_k = false;
@@ -1057,7 +1152,8 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
   K.win_lo = K.win_hi = 0u;
   K.thr = -INFINITY;
   K.thr_idx = INT_MAX;
-  const float min_s = (gmin < INFINITY && gmin > -INFINITY) ? (R.t_one ? gmin : __fdiv_rn(gmin, R.T)) : -INFINITY;
+  const float min_s =
+      (gmin2 < INFINITY && gmin2 > -INFINITY) ? (R.t_one ? gmin2 : __fdiv_rn(gmin2, R.T)) : -INFINITY;
   int hbuf = 0;
 
   // ---- large top-k: exact radix select of the k-th largest penalized logit
@@ -1131,10 +1227,9 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
           atomicAdd(&hist[b], approx_mass16(bits));
         }
       }
-      if (topp) vals4[f] = make_float4(t[0], t[1], t[2], t[3]);
+      vals4[f] = make_float4(t[0], t[1], t[2], t[3]);
     }
   }
-  if (!topp) prefetch();  // the draw recomputes its masses from global memory
   {
     const double cz = cta_warp_sums(ctl, lane_z, lane, warp);  // ctl.wmass = per-warp totals
     if (tid == 0) ctl.cz[0] = cz;
@@ -1145,6 +1240,7 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
   int owner = -1;
   double tloc = 0.0;
   bool crossed = false;
+  uint32_t keep_lo = 1u;  // kept <=> bits(e) >= keep_lo and e > 0
 
   if (topp) {
     // ---- top-p locator: a window of buckets that must contain the boundary
@@ -1186,7 +1282,6 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
       topp_window(ctl, hist, 1, lv, false, z, R.p, tid);
     }
     cluster_sync();  // peers done reading the locator histograms
-    if (!crossed) prefetch();
     if (crossed) {
       // ---- collection: exact mass above the window; window members -> leader
       float lane_above = 0.0f;
@@ -1217,9 +1312,8 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
               const int local = 4 * f + c;
               const float s = scaled(R, penalized_from_global(g, R, bitmap, local));
               if (slot < (uint32_t)kCap) {
-                dsmem_st_f32(dsmem_map(smem_addr(&sm.cand_s[slot]), R.lead), s);
-                dsmem_st_u32(dsmem_map(smem_addr(&sm.cand_i[slot]), R.lead), (uint32_t)(g.base + local));
-                dsmem_st_f32(dsmem_map(smem_addr(&sm.cand_e[slot]), R.lead), t[c]);
+                dsmem_st_f32(dsmem_map(smem_addr(&sm.cand_s[slot]), lead), s);
+                dsmem_st_u32(dsmem_map(smem_addr(&sm.cand_i[slot]), lead), (uint32_t)(g.base + local));
               }
               const uint32_t ms = atomicAdd(&ctl.mem_n, 1u);
               if (ms < (uint32_t)kCap) { sm.mem_s[ms] = s; sm.mem_i[ms] = local; sm.mem_e[ms] = t[c]; }
@@ -1227,20 +1321,19 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
           }
         }
       }
-      prefetch();  // the slice is no longer needed
       {
         const double s = cta_warp_sums(ctl, lane_above, lane, warp);  // ctl.wmass = above masses
-        if (tid == 0) dsmem_st_f64(dsmem_map(smem_addr(&rv.rec_above[g.rank]), R.lead), s);
+        if (tid == 0) dsmem_st_f64(dsmem_map(smem_addr(&rv.rec_above[g.rank]), lead), s);
       }
       cluster_sync();  // barrier: members and above-window masses delivered
       if (leader) {
         float* cand_s = sm.cand_s;
         int32_t* cand_i = sm.cand_i;
-        float* cand_e = sm.cand_e;
-        int32_t* perm = sm.perm;
+        unsigned long long* keys = sm.keys;
         const uint32_t ntot = rv.cand_n;
         const int n = (int)min(ntot, (uint32_t)kCap);
-        leader_sort(n, cand_s, cand_i, perm, tid);
+        for (int i = tid; i < n; i += kThreads) keys[i] = rank_key(cand_s[i], cand_i[i]);
+        bitonic_sort(keys, n, tid);
         if (warp == 0) {
           double before = 0.0;
           for (int r = 0; r < kCluster; ++r) before += rv.rec_above[r];
@@ -1249,7 +1342,7 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
           if (ntot <= (uint32_t)kCap) {
             for (int c0 = 0; c0 < n && j0 < 0; c0 += 32) {
               const int r = c0 + lane;
-              const float er = r < n ? cand_e[perm[r]] : 0.f;
+              const float er = r < n ? exp_shifted(key_value(keys[r]), K.m) : 0.f;
               const double inc = warp_incl_f64((double)er, lane) + run;
               const uint32_t bal = __ballot_sync(0xffffffffu, r < n && er > 0.f && topp_crossed(inc, z, R.p));
               if (bal) j0 = c0 + __ffs(bal) - 1;
@@ -1257,22 +1350,26 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
             }
           }
           if (j0 < 0) j0 = n - 1;  // no crossing inside (or overflow): keep the window
-          const float thr = n > 0 ? cand_s[perm[j0]] : -INFINITY;
-          const int thr_idx = n > 0 ? cand_i[perm[j0]] : INT_MAX;
-          // kept mass per CTA: above-window mass + kept members (rank order)
+          const float thr = n > 0 ? key_value(keys[j0]) : -INFINITY;
+          const int thr_idx = n > 0 ? key_index(keys[j0]) : INT_MAX;
+          // kept mass per CTA: above-window mass + kept members (lane-strided, then combined)
           double kept[kCluster];
 #pragma unroll
-          for (int r = 0; r < kCluster; ++r) kept[r] = rv.rec_above[r];
-          for (int r = 0; r <= j0 && r < n; ++r) {
-            const int owner_r = cand_i[perm[r]] / g.W;
-            const double add = (double)cand_e[perm[r]];
+          for (int r = 0; r < kCluster; ++r) kept[r] = 0.0;
+          for (int r = lane; r <= j0 && r < n; r += 32) {
+            const unsigned long long kk = keys[r];
+            const int owner_r = key_index(kk) / g.W;
+            const double add = (double)exp_shifted(key_value(kk), K.m);
 #pragma unroll
             for (int q = 0; q < kCluster; ++q)
               if (q == owner_r) kept[q] += add;
           }
           double zk = 0.0;
 #pragma unroll
-          for (int r = 0; r < kCluster; ++r) zk += kept[r];
+          for (int r = 0; r < kCluster; ++r) {
+            kept[r] = warp_dsum(kept[r]) + rv.rec_above[r];
+            zk += kept[r];
+          }
           int own;
           double t_own = 0.0;
           pick_owner(kept, u * zk, own, t_own);
@@ -1296,18 +1393,23 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
       owner = ctl.bc_owner;
       tloc = ctl.bc_tloc;
       zkept = ctl.bc_z;
-      // add this CTA's kept members to its per-warp masses (fixed point: order-independent)
+      keep_lo = win_lo;
+      // drop this CTA's members ranked after the threshold element and add
+      // the kept ones to the per-warp masses (fixed point: order-independent)
       if (tid < kWarps) ctl.wfix[tid] = 0ull;
       __syncthreads();
       const int nm = (int)min(ctl.mem_n, (uint32_t)kCap);
       for (int i = tid; i < nm; i += kThreads) {
         const float sm_s = sm.mem_s[i];
         const int li = sm.mem_i[i];
-        if (!(sm_s < K.thr || (sm_s == K.thr && g.base + li > K.thr_idx))) {
+        if (sm_s < K.thr || (sm_s == K.thr && g.base + li > K.thr_idx)) {
+          vals[li] = 0.0f;
+        } else {
           const int w = min(kWarps - 1, (li >> 2) / g.chunk);
           atomicAdd(&ctl.wfix[w], (unsigned long long)llrint((double)sm.mem_e[i] * kFixedScale));
         }
       }
+      fence_proxy_async_smem();  // the zeroed elements may sit in another warp's piece
       __syncthreads();
       if (tid < kWarps) ctl.wmass[tid] += (double)ctl.wfix[tid] * kFixedToReal;
       __syncthreads();
@@ -1321,71 +1423,21 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
     pick_owner(rv.rec_z, u * zkept, owner, tloc);
   }
 
-  // ---- the draw: the owning CTA walks its warps' kept masses in vocabulary order
+  // ---- the draw: the owning CTA picks a warp, the warp walks its piece of the slice
   if (R.greedy || owner < 0) {
+    prefetch();
     if (leader && tid == 0) write_token(a.out_tokens, out_i32, row, gamax);
-  } else if ((int)g.rank == owner) {
-    int wsel = -1;
-    double wpre = 0.0;
-    {
-      double run = 0.0, lastpre = 0.0;
-      int lastw = -1;
-      for (int w = 0; w < kWarps; ++w) {
-        const double x = ctl.wmass[w];
-        if (x > 0.0) { lastw = w; lastpre = run; }
-        if (wsel < 0 && x > 0.0 && run + x > tloc) { wsel = w; wpre = run; }
-        run += x;
-      }
-      if (wsel < 0) { wsel = lastw; wpre = lastpre; }
-    }
+  } else if ((int)g.rank != owner) {
+    prefetch();
+  } else {
+    int wsel;
+    double tw = 0.0;
+    pick_warp(ctl.wmass, tloc, wsel, tw);
     if (warp == wsel) {
-      // rows of 32 float4 slots of this warp's piece, recomputed from global memory
-      const int w_begin = wsel * g.chunk, w_end = min(g.nf4, w_begin + g.chunk);
-      const double tw = tloc - wpre;
-      double run = 0.0;
-      int tok = -1, last_kept = -1;
-      for (int f0 = w_begin; f0 < w_end && tok < 0; f0 += 32) {
-        const int f = f0 + lane;
-        float q[4] = {0.f, 0.f, 0.f, 0.f};
-        if (f < w_end) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) q[c] = kept_mass(g, R, K, bitmap, 4 * f + c);
-        }
-        const float ls = __fadd_rn(__fadd_rn(__fadd_rn(q[0], q[1]), q[2]), q[3]);
-        const double inc = warp_incl_f64((double)ls, lane);
-        const double rowtot = __shfl_sync(0xffffffffu, inc, 31);
-        int lk = -1;
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          if (q[c] > 0.f) lk = g.base + 4 * f + c;
-        for (int o = 16; o; o >>= 1) lk = max(lk, __shfl_xor_sync(0xffffffffu, lk, o));
-        if (lk >= 0) last_kept = lk;
-        if (run + rowtot > tw) {
-          const uint32_t bal = __ballot_sync(0xffffffffu, run + inc > tw && ls > 0.f);
-          if (bal) {
-            const int l = __ffs(bal) - 1;
-            if (lane == l) {
-              double cum = run + inc - (double)ls;
-              int pick = -1, lastc = -1;
-              for (int c = 0; c < 4; ++c) {
-                if (q[c] > 0.f) {
-                  lastc = c;
-                  cum += (double)q[c];
-                  if (pick < 0 && cum > tw) pick = c;
-                }
-              }
-              if (pick < 0) pick = lastc;
-              tok = g.base + 4 * f + pick;
-            }
-            tok = __shfl_sync(0xffffffffu, tok, l);
-          }
-        }
-        run += rowtot;
-      }
-      if (tok < 0) tok = last_kept;
-      if (tok < 0) tok = gamax;  // no kept mass at all (cannot happen for a regular row)
+      const int tok = walk_warp(g, vals4, wsel, keep_lo, tw, lane, gamax);
       if (lane == 0) write_token(a.out_tokens, out_i32, row, tok);
     }
+    prefetch();
   }
   if (debug) {
     for (int i = tid; i < g.len; i += kThreads) {
@@ -1408,8 +1460,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
   sm.bitmap = reinterpret_cast<uint32_t*>(smem + L.bitmap);
   sm.cand_s = reinterpret_cast<float*>(smem + L.cand_s);
   sm.cand_i = reinterpret_cast<int32_t*>(smem + L.cand_i);
-  sm.cand_e = reinterpret_cast<float*>(smem + L.cand_e);
-  sm.perm = reinterpret_cast<int32_t*>(smem + L.perm);
+  sm.keys = reinterpret_cast<unsigned long long*>(smem + L.keys);
   sm.mem_s = reinterpret_cast<float*>(smem + L.mem_s);
   sm.mem_i = reinterpret_cast<int32_t*>(smem + L.mem_i);
   sm.mem_e = reinterpret_cast<float*>(smem + L.mem_e);
@@ -1440,7 +1491,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
   const int ncl = gridDim.x / kCluster;
   const int nrows = a.num_rows;
 
-  // one-time setup: barriers and both receive areas
+  // one-time setup: barriers, both receive areas, the first row's inputs
   if (tid == 0) {
     for (int w = 0; w < kWarps; ++w) mbar_init(&ctl.mbar[w], 1);
     fence_mbar_init();
@@ -1448,6 +1499,10 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
   {
     uint4* r4 = reinterpret_cast<uint4*>(sm.recv);
     for (int i = tid; i < (int)(2 * sizeof(Recv) / 16); i += kThreads) r4[i] = make_uint4(0, 0, 0, 0);
+  }
+  if (cid < nrows) {
+    fetch_row_inputs(a, ctl.rin[0], cid, tid);
+    if (tid < 4) cp_async_wait_all();
   }
   __syncthreads();
   cluster_sync();  // every CTA of the cluster runs and is initialised
@@ -1463,9 +1518,11 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
       for (int i = tid; i < (int)(sizeof(Recv) / 16); i += kThreads) r4[i] = make_uint4(0, 0, 0, 0);
     }
     const int next = (row + ncl < nrows) ? row + ncl : -1;
+    if (next >= 0) fetch_row_inputs(a, ctl.rin[(it & 1u) ^ 1u], next, tid);
     bool prefetched = false;
-    process_row(a, S, g, sm, row, next, it & 1u, tid, prefetched);
+    process_row(a, S, g, sm, row, next, it & 1u, it & (kCluster - 1), tid, prefetched);
     if (!prefetched && next >= 0) issue_chunk(S, g, ctl, sm.vals, next, warp, lane);
+    if (tid < 4) cp_async_wait_all();  // the next row's inputs have landed
   }
   cluster_sync();  // nobody leaves while a peer may still address its shared memory
 }
@@ -1528,6 +1585,11 @@ int ns_sample(const NsSampleArgs* args, void* stream) {
     return fail(NS_ERR_INVALID_ARG, "ns_sample: fewer logits rows than num_rows and no sample_indices");
   if (a.history_offsets && !a.history_ids)
     return fail(NS_ERR_INVALID_ARG, "ns_sample: history_offsets given without history_ids");
+  const uintptr_t rp = reinterpret_cast<uintptr_t>(a.row_params);
+  if (rp % 16 != 0) return fail(NS_ERR_INVALID_ARG, "ns_sample: row_params must be 16-byte aligned");
+  if ((a.history_offsets && reinterpret_cast<uintptr_t>(a.history_offsets) % 8 != 0) ||
+      (a.sample_indices && reinterpret_cast<uintptr_t>(a.sample_indices) % 8 != 0))
+    return fail(NS_ERR_INVALID_ARG, "ns_sample: history_offsets / sample_indices must be 8-byte aligned");
 
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
