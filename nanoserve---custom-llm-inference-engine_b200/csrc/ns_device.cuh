@@ -215,6 +215,48 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
   return d;
 }
 
+// ----------------------------------------------------------------- warp helpers
+__device__ __forceinline__ double warp_dsum(double v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ uint32_t warp_incl_u32(uint32_t v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    uint32_t t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+__device__ __forceinline__ double warp_incl_f64(double v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    double t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+
+// The reference keeps sorted rank j of the top-p pass iff j == 0 or
+// float32(cum[j-1]) <= top_p (sampler.py:66-70); the first rank whose
+// inclusive mass passes this test is the last one kept.
+__device__ __forceinline__ bool topp_crossed(double cum, double z, float p) {
+  return (float)(cum / z) > p;
+}
+
+// Sort key: ascending keys give (value descending, index ascending).
+__device__ __forceinline__ unsigned long long rank_key(float s, int idx) {
+  return ((unsigned long long)(~f2key(s)) << 32) | (uint32_t)idx;
+}
+__device__ __forceinline__ float key_value(unsigned long long k) { return key2f(~(uint32_t)(k >> 32)); }
+__device__ __forceinline__ int key_index(unsigned long long k) { return (int)(uint32_t)k; }
+
+__device__ __forceinline__ void write_token(void* out, bool i32, int row, int tok) {
+  if (i32) reinterpret_cast<int32_t*>(out)[row] = tok;
+  else reinterpret_cast<int64_t*>(out)[row] = tok;
+}
+
 // ----------------------------------------------------------------- Philox4x32-10
 // Counter-based generator of Salmon, Moraes, Dror and Shaw, "Parallel random
 // numbers: as easy as 1, 2, 3" (SC'11): 10 rounds of the 4x32 Philox

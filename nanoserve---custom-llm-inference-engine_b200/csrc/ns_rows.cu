@@ -1,0 +1,1750 @@
+// ns_rows.cu -- B200 (sm_100a) token sampling for large batches: one thread
+// block per row, every row streamed from HBM once.
+//
+// Replaces nanoserve/scheduler/sampler.py:21-89 (Sampler.sample) when the
+// batch has enough rows to occupy the SMs; the cluster kernel in
+// ns_sample.cu serves small batches, unaligned rows and small vocabularies.
+// Design:
+//
+//  * Persistent blocks of 512 threads, two per SM; block b samples rows
+//    b, b+G, b+2G...  Warp w owns the contiguous range [w*W, (w+1)*W) of
+//    every row (W = V/16 rounded up), which it reads as 512-byte pieces,
+//    16 bytes (4 fp32 or 8 bf16 logits) per lane.  Chunk c of a row is the
+//    c-th piece of all 16 ranges, one 8 KB stage of a shared-memory ring.
+//  * Thread t only ever reads the t-th 16 bytes of a stage, so it fills that
+//    slot itself with cp.async, kStages chunks ahead of its reads (one commit
+//    group per chunk).  Nothing ties the warps together while they stream,
+//    and the copies run on into the row's second pass or the next row while
+//    the block is still deciding the current one.
+//  * The first pass gathers everything a row's path needs, so greedy and
+//    top-k rows read HBM exactly once:
+//      GREEDY  temperature 0 and no debug output: first-index argmax
+//              (sampler.py:82-83).
+//      TOPK    0 < top_k <= kTopkMax: the k-th largest of the per-thread
+//              maxima seen so far bounds the k-th largest logit from below;
+//              it is refreshed after chunks 0 and kRefreshAt, and every
+//              element above it goes to its warp's own candidate list.  At
+//              the end the candidates above the final bound are sorted, and
+//              top-k (sampler.py:53-58), top-p (sampler.py:60-73), softmax
+//              and the draw finish on that short list.
+//      GENERAL the rest.  e = exp(s - m0), m0 the first chunk's maximum, is
+//              summed per thread (plain sampling) and, for top-p, also fed to
+//              a histogram of approximate masses keyed on the bits of e
+//              (log-spaced buckets, one 32-bit shared atomic per element).  A
+//              top-p row then takes a second pass through the ring (an L2
+//              re-read, fetched while the histogram is searched) that sums the
+//              exact mass above a window of buckets that must contain the
+//              boundary and collects the window's elements, which are sorted
+//              to decide exactly.
+//  * The draw is an inverse CDF in vocabulary order driven by the row's
+//    uniform: the warp range whose kept-mass prefix passes the target, then
+//    the 512-byte piece inside it (masses recomputed from an L2 re-read of
+//    that range), then the element, walked by one warp.
+//  * Rare cases -- top_k > kTopkMax, candidate-list overflow, a row maximum
+//    far above the first chunk's, NaN/inf rows, debug outputs -- re-read the
+//    row from global memory as often as they need.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <climits>
+#include <mutex>
+#include <string>
+
+#include "../../include/nanoserve_sampler.h"
+#include "ns_device.cuh"
+#include "ns_rows.h"
+
+namespace ns {
+namespace rk {
+
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kStages = 6;                // ring depth (chunks in flight per thread)
+constexpr int kPieceBytes = 512;          // one warp's share of a chunk
+constexpr int kChunkBytes = kWarps * kPieceBytes;
+constexpr int kBins = 4096;               // top-p locator histogram (u32 approximate masses)
+constexpr int kCoarse = 64;               // coarse buckets of kFine fine buckets
+constexpr int kFine = kBins / kCoarse;
+constexpr int kTmBins = 2048;             // per-thread-maximum histogram, quarter binades
+constexpr int kTmShift = 21;
+constexpr int kRadixBins = 2048;          // radix-select level histogram (u32 counts)
+constexpr int kTopkMax = 128;             // largest top_k served by the TOPK path
+constexpr int kRefreshAt = 8;             // TOPK bound refreshes after chunks 0 and 8
+constexpr int kCandCap = 2048;            // candidate / window-member capacity (u64 keys)
+constexpr int kWarpCands = kCandCap / kWarps;  // TOPK: each warp's own candidate list
+constexpr uint32_t kTopFine = 0x4F7FFFFFu;  // first locator level: e = exp(s - m0) in [2^-32, 2^32)
+constexpr int kShFine = 17;                  // 1/64 binade per bucket
+constexpr uint32_t kTopWide = 0x5F7FFFFFu;  // fallback level: e < 2^64, every normal float
+constexpr int kShWide = 19;                  // 1/16 binade per bucket
+constexpr double kSlack = 1.0 + 0x1p-11;  // > 1 / (1 - 2^-12): locator mass error bound
+constexpr int kMinVocab = 24576;          // a row spans more chunks than the ring has stages
+constexpr int kMaxVocab = 196608;
+constexpr int kMaxChunks = (kMaxVocab / kWarps + 127) / 128;  // pieces per warp range (fp32)
+
+// ---------------------------------------------------------------- element formats
+// 16 bytes of a row as logits.
+struct EF32 {
+  static constexpr int kEPT = 4;            // elements per thread per chunk
+  static constexpr int kPiece = 32 * kEPT;  // elements per warp piece
+  using Raw = float4;
+  static __device__ __forceinline__ Raw zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  static __device__ __forceinline__ Raw lds(const unsigned char* p) { return *reinterpret_cast<const float4*>(p); }
+  static __device__ __forceinline__ Raw ldg(const char* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+  static __device__ __forceinline__ void unpack(const Raw& r, float (&x)[kEPT]) {
+    x[0] = r.x;
+    x[1] = r.y;
+    x[2] = r.z;
+    x[3] = r.w;
+  }
+};
+struct EBF16 {
+  static constexpr int kEPT = 8;
+  static constexpr int kPiece = 32 * kEPT;
+  using Raw = uint4;
+  static __device__ __forceinline__ Raw zero() { return make_uint4(0u, 0u, 0u, 0u); }
+  static __device__ __forceinline__ Raw lds(const unsigned char* p) { return *reinterpret_cast<const uint4*>(p); }
+  static __device__ __forceinline__ Raw ldg(const char* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+  // bf16 -> fp32 is exact: the bf16 bits are the high half of the fp32 bits
+  static __device__ __forceinline__ void unpack(const Raw& r, float (&x)[kEPT]) {
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      x[2 * q] = __uint_as_float(w[q] << 16);
+      x[2 * q + 1] = __uint_as_float(w[q] & 0xffff0000u);
+    }
+  }
+};
+
+// ---------------------------------------------------------------- locator masses
+// Approximate mass of one positive normal float: the top 13 of its 24
+// significand bits.  All elements of one locator bucket share their binary
+// exponent, so a bucket's sum of these values, scaled by 2^(exponent - 139),
+// under-estimates its exact mass by less than a factor (1 - 2^-12); a bucket
+// of up to 2^18 elements sums below 2^31.
+__device__ __forceinline__ uint32_t approx_mass13(uint32_t bits) { return ((bits >> 11) & 0xfffu) | 0x1000u; }
+
+// Bucket b of a locator level covers bits of e in [top - (b+1)*2^sh + 1,
+// top - b*2^sh]; top + 1 is a multiple of 2^sh, so each bucket lies inside
+// one binade.
+struct Level {
+  uint32_t top;
+  int sh;
+  __device__ __forceinline__ uint32_t lo_key(int b) const {
+    const uint64_t span = (uint64_t)(b + 1) << sh;
+    return span > (uint64_t)top + 1u ? 0u : top - (uint32_t)span + 1u;
+  }
+  __device__ __forceinline__ uint32_t hi_key(int b) const { return top - ((uint32_t)b << sh); }
+  __device__ __forceinline__ double mass(uint32_t sum13, int b) const {
+    if (sum13 == 0u) return 0.0;
+    // sum13 * 2^(exponent - 139), the power of two built from its bits
+    const int ex = (int)(lo_key(b) >> 23) - 139 + 1023;
+    return (double)sum13 * __longlong_as_double((long long)ex << 52);
+  }
+};
+
+// ---------------------------------------------------------------- shared state
+// One row's inputs, fetched two rows ahead.
+struct __align__(16) RowIn {
+  NsRowParams P;
+  int64_t h[2];
+  int64_t src;
+  int64_t pad;
+};
+
+// Where a row comes from and how often the ring streams it.
+struct RowPlan {
+  const char* src;  // the row in global memory
+  int passes;       // passes through the ring (1, or 2 for top-p rows)
+  int valid;        // the row exists
+};
+
+struct __align__(16) Ctl {
+  RowIn rin[4];
+  RowPlan plan[2];
+  double seg[kWarps];        // kept mass per warp range
+  double piece[kMaxChunks];  // kept mass per piece of the drawn warp range
+  uint32_t red_k[kWarps];
+  uint32_t red_b[kWarps];
+  int32_t red_i[kWarps];
+  int32_t red_j[kWarps];
+  uint32_t red_u[kWarps];
+  uint32_t red_o[kWarps];
+  double red_e[kWarps];
+  double cmass[kCoarse];
+  double pick_t;
+  double dec_z;
+  float sel_est;
+  int sel_found;
+  int sel_lo;
+  int sel_hi;
+  uint32_t sel_before;
+  int pick;
+  uint32_t cand_n;
+  uint32_t list_n;
+  int misc;
+  int misc2;
+  int token;
+  float dec_thr;
+  int dec_thr_idx;
+};
+
+struct Layout {
+  size_t ctl, ring, bitmap, cand, hist, tm, total;
+};
+
+__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) & ~(a - 1); }
+
+__host__ __device__ inline Layout make_layout(int V) {
+  Layout L;
+  size_t o = 0;
+  L.ctl = o;    o = align_up(o + sizeof(Ctl), 128);
+  L.ring = o;   o = align_up(o + (size_t)kStages * kChunkBytes, 16);
+  L.bitmap = o; o = align_up(o + sizeof(uint32_t) * (size_t)((V + 31) / 32), 16);
+  L.cand = o;   o = align_up(o + sizeof(unsigned long long) * kCandCap, 16);
+  L.hist = o;   o = align_up(o + sizeof(uint32_t) * kBins, 16);
+  L.tm = o;     o = align_up(o + sizeof(uint32_t) * kTmBins, 16);
+  L.total = o;
+  return L;
+}
+
+struct Sh {
+  Ctl* ctl;
+  unsigned char* ring;
+  uint32_t* bitmap;
+  unsigned long long* cand;  // TOPK candidates / top-p window members
+  uint32_t* hist;            // locator or radix histogram; TOPK: the final sorted list (u64)
+  uint32_t* tm;              // per-thread-maximum histogram
+};
+
+// One row being sampled, with the row layout shared by every row.
+struct RowCtx {
+  const char* src;
+  int V, W, nch, row;
+  float T, rT, rp, p;
+  int k;  // top-k (0: none)
+  bool t_one, greedy, topp, pen;
+};
+
+// This thread's place in the row layout (the same for every row).
+struct Lane {
+  int tid, lane, warp;
+  int base;  // element index of this thread's first element in chunk 0
+  int nv;    // chunks in which this thread holds elements
+};
+
+template <class E>
+__device__ __forceinline__ Lane make_lane(int V, int W, int tid) {
+  Lane ln;
+  ln.tid = tid;
+  ln.lane = tid & 31;
+  ln.warp = tid >> 5;
+  ln.base = ln.warp * W + ln.lane * E::kEPT;
+  const int ww = max(0, min(W, V - ln.warp * W));  // this warp's range length
+  ln.nv = ww > ln.lane * E::kEPT ? (ww - ln.lane * E::kEPT + E::kPiece - 1) / E::kPiece : 0;
+  return ln;
+}
+
+enum { kGreedy = 0, kTopk = 1, kGeneral = 2 };
+
+__device__ __forceinline__ int row_mode(const NsRowParams& P, int V, bool debug) {
+  const bool greedy = (P.flags & NS_ROW_GREEDY) != 0u;
+  if (greedy && !debug) return kGreedy;
+  const int k = (P.top_k > 0 && P.top_k < V) ? P.top_k : 0;
+  return (k > 0 && k <= kTopkMax) ? kTopk : kGeneral;
+}
+
+__device__ __forceinline__ float scaled(const RowCtx& R, float x) {
+  return R.t_one ? x : div_by_const(x, R.T, R.rT);
+}
+
+// Smallest float c <= b with RN(c/T) == RN(b/T): the lower end of the set of
+// logits whose scaled value is at least RN(b/T).
+__device__ __noinline__ float lower_preimage(const RowCtx& R, float b) {
+  if (R.t_one || !(b > -INFINITY) || !(b < INFINITY)) return b;
+  const float target = div_by_const(b, R.T, R.rT);
+  float c = b;
+  for (int i = 0; i < 64; ++i) {
+    const float d = nextafterf(c, -INFINITY);
+    if (div_by_const(d, R.T, R.rT) == target) c = d; else return c;
+  }
+  return -INFINITY;
+}
+
+// The thread's 16 bytes of a row as penalized logits (sampler.py:31-38).
+template <class E, bool PEN>
+__device__ __forceinline__ void penalized(const uint32_t* bitmap, float rp, const typename E::Raw& raw, int idx0,
+                                          float (&x)[E::kEPT]) {
+  E::unpack(raw, x);
+  if (PEN) {
+    const uint32_t m = (bitmap[idx0 >> 5] >> (idx0 & 31)) & ((1u << E::kEPT) - 1u);
+    if (m) {
+#pragma unroll
+      for (int j = 0; j < E::kEPT; ++j)
+        if ((m >> j) & 1u) x[j] = penalize(x[j], rp);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- the ring
+// Where this thread's refills come from during one pass over a row, offset
+// to its own 16 bytes: chunk c + kStages of the pass if that is still inside
+// it (`cur`), else chunk c + kStages - nch of what follows the pass
+// (`after`: the row's second pass or the next row).  nullptr: nothing.
+struct Feed {
+  const char* cur;
+  const char* after;
+};
+
+// Wait until this thread's copy kStages - 1 groups back has landed.
+__device__ __forceinline__ void cp_async_wait_ring() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(kStages - 1) : "memory");
+}
+
+__device__ __forceinline__ unsigned char* stage_slot(unsigned char* ring, int stage, int tid) {
+  return ring + stage * kChunkBytes + tid * 16;
+}
+
+// The stage at `stage` held chunk c of the current pass; refill this
+// thread's slot of it kStages chunks further on and commit the group (empty
+// when there is nothing to fetch).
+__device__ __forceinline__ void ring_refill(const Feed& f, unsigned char* ring, int stage, int c, int nch,
+                                            const Lane& ln) {
+  c += kStages;
+  const char* src = f.cur;
+  if (c >= nch) {
+    c -= nch;
+    src = f.after;
+  }
+  if (src != nullptr && c < ln.nv) cp_async16(stage_slot(ring, stage, ln.tid), src + c * kPieceBytes);
+  cp_async_commit();
+}
+
+// This thread's bytes of row `src` (16-byte aligned: the host admits only
+// such rows).
+template <class E>
+__device__ __forceinline__ const char* lane_src(const char* src, const Lane& ln) {
+  return src + (size_t)ln.base * (sizeof(typename E::Raw) / E::kEPT);
+}
+
+// Refill sources for the first pass over the block's i-th row, and for its
+// second pass (`wanted` false: the second pass is only drained).
+template <class E>
+__device__ __forceinline__ Feed feed_first(const Ctl& ctl, int i, const Lane& ln) {
+  const RowPlan& p = ctl.plan[i & 1];
+  const RowPlan& n = ctl.plan[(i + 1) & 1];
+  Feed f;
+  f.cur = lane_src<E>(p.src, ln);
+  f.after = p.passes == 2 ? f.cur : (n.valid ? lane_src<E>(n.src, ln) : nullptr);
+  return f;
+}
+template <class E>
+__device__ __forceinline__ Feed feed_second(const Ctl& ctl, int i, const Lane& ln, bool wanted) {
+  const RowPlan& p = ctl.plan[i & 1];
+  const RowPlan& n = ctl.plan[(i + 1) & 1];
+  Feed f;
+  f.cur = wanted ? lane_src<E>(p.src, ln) : nullptr;
+  f.after = n.valid ? lane_src<E>(n.src, ln) : nullptr;
+  return f;
+}
+
+// Prologue: the first kStages chunks of the block's first row.
+template <class E>
+__device__ __forceinline__ void ring_start(const Ctl& ctl, unsigned char* ring, const Lane& ln) {
+  const RowPlan& pl = ctl.plan[0];
+  const char* src = lane_src<E>(pl.src, ln);
+  for (int c = 0; c < kStages; ++c) {
+    if (pl.valid && c < ln.nv) cp_async16(stage_slot(ring, c, ln.tid), src + c * kPieceBytes);
+    cp_async_commit();
+  }
+}
+
+// One pass of the current row through the ring: body(c, x, idx0, live) for
+// every chunk c with this thread's penalized logits; the penalized values are
+// also written to pen_out when given.
+template <class E, bool PEN, class F>
+__device__ __forceinline__ void ring_pass(const Sh& sh, const Lane& ln, const Feed& fd, int nch, int& stage, float rp,
+                                          float* pen_out, F&& body) {
+  constexpr int EPT = E::kEPT;
+  for (int c = 0; c < nch; ++c) {
+    cp_async_wait_ring();
+    const bool live = c < ln.nv;
+    const typename E::Raw raw = live ? E::lds(stage_slot(sh.ring, stage, ln.tid)) : E::zero();
+    ring_refill(fd, sh.ring, stage, c, nch, ln);
+    stage = stage + 1 == kStages ? 0 : stage + 1;
+    const int idx0 = ln.base + c * E::kPiece;
+    float x[EPT];
+    if (live) {
+      penalized<E, PEN>(sh.bitmap, rp, raw, idx0, x);
+      if (pen_out) {
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) pen_out[idx0 + j] = x[j];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < EPT; ++j) x[j] = -INFINITY;
+    }
+    body(c, x, idx0, live);
+  }
+}
+
+// Consume a second pass nobody needs without fetching it.
+__device__ __noinline__ void drain_pass(const Sh& sh, const Lane& ln, const Feed& fd, int nch, int& stage) {
+  for (int c = 0; c < nch; ++c) {
+    cp_async_wait_ring();
+    ring_refill(fd, sh.ring, stage, c, nch, ln);
+    stage = stage + 1 == kStages ? 0 : stage + 1;
+  }
+}
+
+// Calls f(c, x, idx0, live) for every chunk c of the row with this thread's
+// penalized logits, re-read from global memory (four chunks in flight).
+template <class E, class F>
+__device__ __forceinline__ void global_pass(const RowCtx& R, const uint32_t* bitmap, int tid, F&& f) {
+  constexpr int EPT = E::kEPT, U = 4;
+  const Lane ln = make_lane<E>(R.V, R.W, tid);
+  const char* src = lane_src<E>(R.src, ln);
+  for (int c0 = 0; c0 < R.nch; c0 += U) {
+    typename E::Raw raw[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) raw[u] = (c0 + u < ln.nv) ? E::ldg(src + (c0 + u) * kPieceBytes) : E::zero();
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u;
+      if (c < R.nch) {
+        const int idx0 = ln.base + c * E::kPiece;
+        const bool live = c < ln.nv;
+        float x[EPT];
+        if (live) {
+          if (R.pen) penalized<E, true>(bitmap, R.rp, raw[u], idx0, x);
+          else penalized<E, false>(bitmap, R.rp, raw[u], idx0, x);
+        } else {
+#pragma unroll
+          for (int j = 0; j < EPT; ++j) x[j] = -INFINITY;
+        }
+        f(c, x, idx0, live);
+      }
+    }
+  }
+}
+
+// Threads 0..3 copy row `row`'s inputs (64 bytes) into `dst` with plain
+// loads; cp.async is kept for the ring, whose group count must stay exact.
+__device__ __forceinline__ void fetch_row_inputs(const NsSampleArgs& a, RowIn& dst, int row, int tid) {
+  if (tid >= 4) return;
+  uint4 v;
+  if (tid < 2) {
+    v = __ldg(reinterpret_cast<const uint4*>(&a.row_params[row]) + tid);
+  } else {
+    int64_t x0, x1 = 0;
+    if (tid == 2) {
+      x0 = a.history_offsets ? a.history_offsets[row] : 0;
+      x1 = a.history_offsets ? a.history_offsets[row + 1] : 0;
+    } else {
+      x0 = a.sample_indices ? a.sample_indices[row] : row;
+    }
+    v = make_uint4((uint32_t)x0, (uint32_t)((uint64_t)x0 >> 32), (uint32_t)x1, (uint32_t)((uint64_t)x1 >> 32));
+  }
+  reinterpret_cast<uint4*>(&dst)[tid] = v;
+}
+
+// Plan of this block's i-th row (global row `row`), from its fetched inputs.
+__device__ void make_plan(const NsSampleArgs& a, Ctl& ctl, int i, int row, bool debug) {
+  RowPlan& pl = ctl.plan[i & 1];
+  if (row >= a.num_rows) {
+    pl.valid = 0;
+    return;
+  }
+  const RowIn& in = ctl.rin[i & 3];
+  int64_t src = in.src;
+  if (src < 0 || src >= a.num_logit_rows) src = 0;
+  const size_t esize = a.logits_dtype == NS_DTYPE_BF16 ? 2 : 4;
+  pl.src = static_cast<const char*>(a.logits) + (size_t)src * (size_t)a.logits_row_stride * esize;
+  const int mode = row_mode(in.P, a.vocab_size, debug);
+  pl.passes = (mode == kGeneral && (in.P.flags & NS_ROW_TOP_P)) ? 2 : 1;
+  pl.valid = 1;
+}
+
+// ---------------------------------------------------------------- block reductions
+// Block-wide exclusive scan of one u32 per thread (thread 0 first).
+__device__ uint32_t block_excl_u32(Ctl& ctl, uint32_t v, uint32_t& total, int tid) {
+  const int lane = tid & 31, warp = tid >> 5;
+  const uint32_t inc = warp_incl_u32(v, lane);
+  if (lane == 31) ctl.red_u[warp] = inc;
+  __syncthreads();
+  uint32_t wpre = 0, tot = 0;
+  for (int w = 0; w < kWarps; ++w) {
+    const uint32_t x = ctl.red_u[w];
+    if (w < warp) wpre += x;
+    tot += x;
+  }
+  __syncthreads();
+  total = tot;
+  return wpre + inc - v;
+}
+
+__device__ double block_dsum(Ctl& ctl, double v, int tid) {
+  const double w = warp_dsum(v);
+  if ((tid & 31) == 0) ctl.red_e[tid >> 5] = w;
+  __syncthreads();
+  double s = 0.0;
+  for (int i = 0; i < kWarps; ++i) s += ctl.red_e[i];
+  __syncthreads();
+  return s;
+}
+
+// Per-warp-range totals of per-thread masses into ctl.seg, and their sum.
+__device__ double block_segments(Ctl& ctl, double v, int tid) {
+  const double w = warp_dsum(v);
+  if ((tid & 31) == 0) ctl.seg[tid >> 5] = w;
+  __syncthreads();
+  double s = 0.0;
+  for (int i = 0; i < kWarps; ++i) s += ctl.seg[i];
+  __syncthreads();
+  return s;
+}
+
+// Row statistics after the first pass: NaN-propagating maximum with its first
+// index, the row total of the per-thread masses `z` (also kept per warp range
+// in ctl.seg) and whether any e left the locator level above (flag bit 0) or
+// below (bit 1).
+struct Stats {
+  float mx;
+  bool nan;
+  int arg;
+  double z;
+  bool over;
+  bool lumped;
+};
+__device__ Stats block_stats(Ctl& ctl, float v, int arg, double z, uint32_t flags, int tid) {
+  const int lane = tid & 31, warp = tid >> 5;
+  const bool nan = (v != v);
+  const uint32_t k = nan ? 0u : f2key(v);
+  const uint32_t wk = __reduce_max_sync(0xffffffffu, k);
+  const uint32_t wi = __reduce_min_sync(0xffffffffu, k == wk ? (uint32_t)arg : 0x7fffffffu);
+  const bool wn = __any_sync(0xffffffffu, nan);
+  const uint32_t wo = __reduce_or_sync(0xffffffffu, flags);
+  const double wz = warp_dsum(z);
+  if (lane == 0) {
+    ctl.red_k[warp] = wn ? 0xffffffffu : wk;
+    ctl.red_i[warp] = (int)wi;
+    ctl.red_o[warp] = wo;
+    ctl.seg[warp] = wz;
+  }
+  __syncthreads();
+  uint32_t ck = 0u, co = 0u;
+  int ci = INT_MAX;
+  double cz = 0.0;
+  for (int w = 0; w < kWarps; ++w) {
+    const uint32_t kk = ctl.red_k[w];
+    if (kk > ck) {
+      ck = kk;
+      ci = ctl.red_i[w];
+    } else if (kk == ck) {
+      ci = min(ci, ctl.red_i[w]);
+    }
+    co |= ctl.red_o[w];
+    cz += ctl.seg[w];
+  }
+  __syncthreads();
+  Stats S;
+  S.nan = (ck == 0xffffffffu);
+  S.mx = S.nan ? __int_as_float(0x7fc00000) : key2f(ck);
+  S.arg = ci;
+  S.z = cz;
+  S.over = (co & 1u) != 0u;
+  S.lumped = (co & 2u) != 0u;
+  return S;
+}
+
+// Bitonic sort of keys[0, n) ascending in place (n <= kCandCap), whole block.
+__device__ void bitonic_sort(unsigned long long* keys, int n, int tid) {
+  int np = 1;
+  while (np < n) np <<= 1;
+  for (int i = n + tid; i < np; i += kThreads) keys[i] = ~0ull;
+  __syncthreads();
+  for (int k = 2; k <= np; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < np; i += kThreads) {
+        const int l = i ^ j;
+        if (l > i) {
+          const unsigned long long a = keys[i], b = keys[l];
+          const bool up = (i & k) == 0;
+          if ((a > b) == up) {
+            keys[i] = b;
+            keys[l] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Sort keys[0, n) ascending (n <= 32 * NPL) with one warp, in registers
+// (bitonic network; element i lives in lane i % 32, register i / 32).
+template <int NPL>
+__device__ __forceinline__ void warp_sort(unsigned long long* keys, int n, int lane) {
+  unsigned long long v[NPL];
+#pragma unroll
+  for (int r = 0; r < NPL; ++r) {
+    const int i = r * 32 + lane;
+    v[r] = i < n ? keys[i] : ~0ull;
+  }
+#pragma unroll
+  for (int k = 2; k <= 32 * NPL; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= 32) {
+        const int jr = j >> 5;
+#pragma unroll
+        for (int r = 0; r < NPL; ++r) {
+          if ((r & jr) == 0) {
+            const int r2 = r | jr;
+            const bool up = ((r * 32 + lane) & k) == 0;
+            const unsigned long long a = v[r], b = v[r2];
+            const bool sw = (a > b) == up;
+            v[r] = sw ? b : a;
+            v[r2] = sw ? a : b;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < NPL; ++r) {
+          const unsigned long long o = __shfl_xor_sync(0xffffffffu, v[r], j);
+          const bool up = ((r * 32 + lane) & k) == 0;
+          const bool lower = (lane & j) == 0;
+          const unsigned long long mn = v[r] < o ? v[r] : o, mx = v[r] < o ? o : v[r];
+          v[r] = (lower == up) ? mn : mx;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < NPL; ++r) {
+    const int i = r * 32 + lane;
+    if (i < n) keys[i] = v[r];
+  }
+}
+
+// Sort keys[0, n) ascending: one warp in registers for short lists, the
+// whole block otherwise.  Whole block; ends with a barrier.
+__device__ void sort_keys(unsigned long long* keys, int n, int tid) {
+  if (n <= 128) {
+    if (tid < 32) warp_sort<4>(keys, n, tid);
+    __syncthreads();
+  } else if (n <= 256) {
+    if (tid < 32) warp_sort<8>(keys, n, tid);
+    __syncthreads();
+  } else {
+    bitonic_sort(keys, n, tid);
+  }
+}
+
+// Append keys to a block-shared list (warp-aggregated slots); entries past
+// `cap` are counted but dropped.
+__device__ __forceinline__ void list_append(unsigned long long* list, uint32_t* count, bool take,
+                                            unsigned long long key, int cap, int lane) {
+  const uint32_t bal = __ballot_sync(0xffffffffu, take);
+  if (bal) {
+    const int first = __ffs(bal) - 1;
+    uint32_t base = 0;
+    if (lane == first) base = atomicAdd(count, (uint32_t)__popc(bal));
+    base = __shfl_sync(0xffffffffu, base, first);
+    if (take) {
+      const uint32_t slot = base + (uint32_t)__popc(bal & ((1u << lane) - 1u));
+      if (slot < (uint32_t)cap) list[slot] = key;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- top-k bound
+// The k-th largest per-thread maximum (a logit before temperature), rounded
+// down to its quarter binade and extended to every logit whose scaled value
+// ties with it: a lower bound for the k-th largest scaled logit of the row.
+// Whole block.
+__device__ __noinline__ float topk_bound(const RowCtx& R, Ctl& ctl, uint32_t* tm, float tmax, int tid) {
+  for (int b = tid; b < kTmBins; b += kThreads) tm[b] = 0u;
+  __syncthreads();
+  if (tid == 0) ctl.misc = -1;
+  if (tmax == tmax) atomicAdd(&tm[f2key(tmax) >> kTmShift], 1u);
+  __syncthreads();
+  // thread t owns buckets [kTmBins - 4(t+1), kTmBins - 4t), scanned from the top
+  uint32_t cnt[4];
+  uint32_t s = 0;
+  const int bhi = kTmBins - 1 - 4 * tid;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    cnt[j] = tm[bhi - j];
+    s += cnt[j];
+  }
+  uint32_t tot;
+  const uint32_t pre = block_excl_u32(ctl, s, tot, tid);
+  const uint32_t k = (uint32_t)R.k;
+  if (pre < k && pre + s >= k) {
+    uint32_t run = pre;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      run += cnt[j];
+      if (run >= k) {
+        ctl.misc = bhi - j;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  const int b = ctl.misc;
+  const uint32_t bkey = b < 0 ? 0u : (uint32_t)b << kTmShift;
+  const float bound = (b < 0 || bkey < 0x00800000u) ? -INFINITY : key2f(bkey);
+  return lower_preimage(R, bound);
+}
+
+// ---------------------------------------------------------------- radix select
+// k-th largest penalized logit by a 3-level radix select over its key
+// (11/11/10 bits), re-reading the row three times.  Whole block.
+template <class E>
+__device__ float radix_select(const RowCtx& R, const Sh& sh, int tid) {
+  Ctl& ctl = *sh.ctl;
+  uint32_t* h = sh.hist;
+  uint32_t prefix = 0u, krem = (uint32_t)R.k;
+  const int shifts[3] = {21, 10, 0};
+  const int widths[3] = {11, 11, 10};
+  for (int lvl = 0; lvl < 3; ++lvl) {
+    const int shl = shifts[lvl], wd = widths[lvl];
+    const uint32_t nbm = (1u << wd) - 1u;
+    for (int b = tid; b < kRadixBins; b += kThreads) h[b] = 0u;
+    __syncthreads();
+    if (tid == 0) ctl.misc = -1;
+    global_pass<E>(R, sh.bitmap, tid, [&](int, const float(&x)[E::kEPT], int, bool live) {
+      if (!live) return;
+#pragma unroll
+      for (int j = 0; j < E::kEPT; ++j) {
+        const uint32_t key = f2key(x[j]);
+        if (lvl > 0 && (key >> (shl + wd)) != prefix) continue;
+        atomicAdd(&h[nbm - ((key >> shl) & nbm)], 1u);
+      }
+    });
+    __syncthreads();
+    // bucket 0 holds the largest keys; thread t owns buckets [4t, 4t+4)
+    uint32_t cnt[4], s = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      cnt[j] = h[4 * tid + j];
+      s += cnt[j];
+    }
+    uint32_t tot;
+    const uint32_t pre = block_excl_u32(ctl, s, tot, tid);
+    if (pre < krem && pre + s >= krem) {
+      uint32_t run = pre;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (run + cnt[j] >= krem) {
+          ctl.misc = 4 * tid + j;
+          ctl.sel_before = run;
+          break;
+        }
+        run += cnt[j];
+      }
+    }
+    __syncthreads();
+    const int b = ctl.misc;
+    if (b < 0) return -INFINITY;  // fewer than k elements (k < V makes this impossible)
+    krem -= ctl.sel_before;
+    prefix = (prefix << wd) | (nbm - (uint32_t)b);
+    __syncthreads();
+  }
+  return key2f(prefix);
+}
+
+// ---------------------------------------------------------------- top-p window
+// Reference rule (sampler.py:66-70): sorted rank j is kept iff j == 0 or
+// float32(cum[j-1]) <= top_p; topp_crossed() is the test on inclusive mass.
+// Finds the bucket window [lo, hi] of level `lv` that must contain the first
+// crossing, given that each bucket's approximate mass is within a factor
+// (1 - 2^-12) of its exact mass, plus an estimate of its element count.
+// `base` is the exact mass above the level's range, `z` the row total.
+__device__ __noinline__ void topp_window(Ctl& ctl, const uint32_t* h, const Level& lv, double base, double z,
+                                         float p, int tid) {
+  const int lane = tid & 31, warp = tid >> 5;
+  {
+    // coarse sums: 8 threads per coarse bucket, 8 fine buckets each
+    const int c = tid >> 3;
+    double m = 0.0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int b = tid * 8 + j;
+      m += lv.mass(h[b], b);
+    }
+#pragma unroll
+    for (int o = 4; o; o >>= 1) m += __shfl_xor_sync(0xffffffffu, m, o);
+    if ((tid & 7) == 0) ctl.cmass[c] = m;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    double cm[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) cm[hh] = ctl.cmass[hh * 32 + lane];
+    // first coarse buckets where the upper (slack) and the lower estimate cross
+    int c_lo = -1, c_hi = -1;
+    double run = base, pre_lo = 0.0;
+    for (int hh = 0; hh < 2; ++hh) {
+      const double inc = warp_incl_f64(cm[hh], lane) + run;
+      const uint32_t bl = __ballot_sync(0xffffffffu, topp_crossed(inc * kSlack, z, p));
+      const uint32_t bh = __ballot_sync(0xffffffffu, topp_crossed(inc, z, p));
+      if (c_lo < 0 && bl) {
+        const int l = __ffs(bl) - 1;
+        c_lo = hh * 32 + l;
+        pre_lo = __shfl_sync(0xffffffffu, inc - cm[hh], l);
+      }
+      if (c_hi < 0 && bh) c_hi = hh * 32 + __ffs(bh) - 1;
+      run = __shfl_sync(0xffffffffu, inc, 31);
+    }
+    int found = (c_lo >= 0);
+    int b_lo = 0, b_hi = 0;
+    float est = 0.f;
+    if (found) {
+      if (c_hi < 0) c_hi = kCoarse - 1;
+      double frun = pre_lo;
+      int fl = -1, fh = -1;
+      double est_d = 0.0;
+      for (int c = c_lo; c <= c_hi && fh < 0; ++c) {
+        for (int hh = 0; hh < 2 && fh < 0; ++hh) {
+          const int b = c * kFine + hh * 32 + lane;
+          const double m = lv.mass(h[b], b);
+          const double inc = warp_incl_f64(m, lane) + frun;
+          const uint32_t bl = __ballot_sync(0xffffffffu, topp_crossed(inc * kSlack, z, p));
+          const uint32_t bh = __ballot_sync(0xffffffffu, topp_crossed(inc, z, p));
+          const int flo = (fl < 0 && bl) ? c * kFine + hh * 32 + (__ffs(bl) - 1) : fl;
+          const int fhi = bh ? c * kFine + hh * 32 + (__ffs(bh) - 1) : -1;
+          // elements in the window ~ mass / smallest value of the bucket
+          const bool inwin = (flo >= 0) && b >= flo && (fhi < 0 || b <= fhi);
+          const double e_bot = (double)__uint_as_float(lv.lo_key(b));
+          est_d += warp_dsum((inwin && m > 0.0 && e_bot > 0.0) ? m / e_bot : 0.0);
+          fl = flo;
+          fh = fhi;
+          frun = __shfl_sync(0xffffffffu, inc, 31);
+        }
+      }
+      if (fl < 0) fl = c_lo * kFine;
+      if (fh < 0) fh = c_hi * kFine + kFine - 1;
+      if (fl > fh) fl = fh;
+      b_lo = fl;
+      b_hi = fh;
+      est = (float)(est_d * 1.001 + 1.0);
+    }
+    if (lane == 0) {
+      ctl.sel_found = found;
+      ctl.sel_lo = b_lo;
+      ctl.sel_hi = b_hi;
+      ctl.sel_est = est;
+    }
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------- the draw
+// Which elements survive filtering, and their masses e = exp(s - m0).
+struct Keep {
+  float m0;
+  bool have_k;  // top-k by threshold: s >= thr_k
+  float thr_k;
+  bool window;  // top-p decided inside [win_lo, win_hi]
+  uint32_t win_lo, win_hi;
+  float thr;    // last kept (s, idx) inside the window
+  int thr_idx;
+  __device__ __forceinline__ float mass(float s) const {
+    return (have_k && !(s >= thr_k)) ? 0.0f : exp_shifted(s, m0);
+  }
+  __device__ __forceinline__ bool kept(float s, float e, int idx) const {
+    if (have_k && !(s >= thr_k)) return false;
+    if (!window) return true;
+    const uint32_t bits = __float_as_uint(e);
+    if (bits > win_hi) return true;
+    if (bits < win_lo || bits == 0u) return false;
+    return s > thr || (s == thr && idx <= thr_idx);
+  }
+};
+
+// Kept masses of 16 bytes of logits (`valid` false: all zero).
+template <class E>
+__device__ __forceinline__ void kept_masses(const RowCtx& R, const uint32_t* bitmap, const Keep& K,
+                                            const typename E::Raw& raw, int idx0, bool valid, float (&q)[E::kEPT]) {
+  if (valid) {
+    float x[E::kEPT];
+    if (R.pen) penalized<E, true>(bitmap, R.rp, raw, idx0, x);
+    else penalized<E, false>(bitmap, R.rp, raw, idx0, x);
+#pragma unroll
+    for (int j = 0; j < E::kEPT; ++j) {
+      const float s = scaled(R, x[j]);
+      const float e = K.mass(s);
+      q[j] = (e > 0.f && K.kept(s, e, idx0 + j)) ? e : 0.f;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < E::kEPT; ++j) q[j] = 0.f;
+  }
+}
+
+// The inverse-CDF draw in vocabulary order over the kept masses, whole block:
+// the warp range whose mass prefix (ctl.seg) passes `target`, then the piece
+// inside it (masses recomputed from a re-read of the range), then the
+// element, walked by warp 0.  Falls back to the last kept element when
+// rounding leaves the target past the total, then to `fallback`.
+template <class E>
+__device__ __noinline__ int draw_token(const RowCtx& R, const Sh& sh, const Keep& K, double target, int fallback,
+                                       int tid) {
+  constexpr int kPer = (kMaxChunks + kWarps - 1) / kWarps;  // pieces per warp at most
+  Ctl& ctl = *sh.ctl;
+  const int lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    double run = 0.0, t = 0.0;
+    int pick = -1, last = -1;
+    for (int w = 0; w < kWarps; ++w) {
+      const double m = ctl.seg[w];
+      if (m > 0.0) last = w;
+      if (pick < 0 && m > 0.0 && target < run + m) {
+        pick = w;
+        t = target - run;
+      }
+      run += m;
+    }
+    if (pick < 0) {
+      pick = last;
+      t = 1e300;
+    }
+    ctl.pick = pick;
+    ctl.pick_t = t;
+  }
+  __syncthreads();
+  const int wr = ctl.pick;
+  const double t1 = ctl.pick_t;
+  if (wr < 0) return fallback;
+  const int ww = max(0, min(R.W, R.V - wr * R.W));
+  const int npieces = (ww + E::kPiece - 1) / E::kPiece;
+  const char* base = R.src + (size_t)wr * R.W * (sizeof(typename E::Raw) / E::kEPT);
+  {
+    // piece masses: warp w takes pieces w, w + 16, ...; all loads first
+    typename E::Raw raw[kPer];
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      const int off = (warp + q * kWarps) * E::kPiece + lane * E::kEPT;
+      raw[q] = off < ww ? E::ldg(base + (size_t)off * (sizeof(typename E::Raw) / E::kEPT)) : E::zero();
+    }
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      const int p = warp + q * kWarps;
+      if (p < npieces) {
+        const int off = p * E::kPiece + lane * E::kEPT;
+        float m[E::kEPT];
+        kept_masses<E>(R, sh.bitmap, K, raw[q], wr * R.W + off, off < ww, m);
+        float ls = 0.f;
+#pragma unroll
+        for (int j = 0; j < E::kEPT; ++j) ls = __fadd_rn(ls, m[j]);
+        const double ps = warp_dsum((double)ls);
+        if (lane == 0) ctl.piece[p] = ps;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int pick = -1, last = -1;
+    double t2 = 0.0, run = 0.0;
+    for (int p0 = 0; p0 < npieces; p0 += 32) {
+      const int p = p0 + lane;
+      const double m = p < npieces ? ctl.piece[p] : 0.0;
+      const double inc = warp_incl_f64(m, lane) + run;
+      const uint32_t pos = __ballot_sync(0xffffffffu, m > 0.0);
+      const uint32_t hit = __ballot_sync(0xffffffffu, m > 0.0 && t1 < inc);
+      if (pos) last = p0 + 31 - __clz(pos);
+      if (pick < 0 && hit) {
+        const int l = __ffs(hit) - 1;
+        pick = p0 + l;
+        t2 = t1 - __shfl_sync(0xffffffffu, inc - m, l);
+      }
+      run = __shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (pick < 0) {
+      pick = last;
+      t2 = 1e300;
+    }
+    int tok = fallback;
+    if (pick >= 0) {
+      const int off = pick * E::kPiece + lane * E::kEPT;
+      const int idx0 = wr * R.W + off;
+      const typename E::Raw raw =
+          off < ww ? E::ldg(base + (size_t)off * (sizeof(typename E::Raw) / E::kEPT)) : E::zero();
+      float q[E::kEPT];
+      kept_masses<E>(R, sh.bitmap, K, raw, idx0, off < ww, q);
+      float ls = 0.f;
+      int lk = -1;
+#pragma unroll
+      for (int j = 0; j < E::kEPT; ++j) {
+        ls = __fadd_rn(ls, q[j]);
+        if (q[j] > 0.f) lk = idx0 + j;
+      }
+      const double inc = warp_incl_f64((double)ls, lane);
+      const uint32_t bal = __ballot_sync(0xffffffffu, inc > t2 && ls > 0.f);
+      if (bal) {
+        const int l = __ffs(bal) - 1;
+        int mine = -1;
+        if (lane == l) {
+          double cum = inc - (double)ls;
+          int pk = -1, lastc = -1;
+#pragma unroll
+          for (int j = 0; j < E::kEPT; ++j) {
+            if (q[j] > 0.f) {
+              lastc = j;
+              cum += (double)q[j];
+              if (pk < 0 && cum > t2) pk = j;
+            }
+          }
+          if (pk < 0) pk = lastc;
+          mine = idx0 + pk;
+        }
+        tok = __shfl_sync(0xffffffffu, mine, l);
+      } else {
+        const int lastk = (int)__reduce_max_sync(0xffffffffu, (uint32_t)(lk + 1)) - 1;
+        if (lastk >= 0) tok = lastk;
+      }
+    }
+    if (lane == 0) ctl.token = tok;
+  }
+  __syncthreads();
+  return ctl.token;
+}
+
+// ---------------------------------------------------------------- one row
+template <class E>
+__device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, const Lane& ln, int& stage, int i,
+                                           int row, int nch, int W) {
+  constexpr int EPT = E::kEPT;
+  const int tid = ln.tid, lane = ln.lane, warp = ln.warp;
+  Ctl& ctl = *sh.ctl;
+  uint32_t* const status = a.status;
+  const int V = a.vocab_size;
+  const bool debug = (a.out_filtered != nullptr) || (a.out_probs != nullptr);
+  const bool out_i32 = (a.out_dtype == NS_OUT_I32);
+  const RowIn& in = ctl.rin[i & 3];
+  const NsRowParams P = in.P;
+  RowCtx R;
+  R.src = ctl.plan[i & 1].src;
+  R.V = V;
+  R.W = W;
+  R.nch = nch;
+  R.row = row;
+  R.greedy = (P.flags & NS_ROW_GREEDY) != 0u;
+  R.T = R.greedy ? 1.0f : P.temperature;
+  R.rT = __frcp_rn(R.T);
+  R.t_one = (R.T == 1.0f);
+  R.topp = (P.flags & NS_ROW_TOP_P) != 0u;
+  R.p = P.top_p;
+  R.k = (P.top_k > 0 && P.top_k < V) ? P.top_k : 0;
+  R.rp = P.repetition_penalty;
+  const int64_t h0 = in.h[0], h1 = in.h[1];
+  R.pen = (P.flags & NS_ROW_PENALTY) != 0u && a.history_offsets && h1 > h0;
+  const bool ring2 = ctl.plan[i & 1].passes == 2;
+  int mode = row_mode(P, V, debug);
+  float* const pen_out = a.out_penalized ? a.out_penalized + (int64_t)row * V : nullptr;
+  const int64_t out_off = (int64_t)row * V;
+
+  // ---------------- setup: penalty bitmap, histograms, counters
+  const bool want_hist = (mode == kGeneral) && R.topp && R.k == 0;
+  if (R.pen)
+    for (int w = tid; w < (V + 31) / 32; w += kThreads) sh.bitmap[w] = 0u;
+  if (want_hist)
+    for (int b = tid; b < kBins / 4; b += kThreads) reinterpret_cast<uint4*>(sh.hist)[b] = make_uint4(0, 0, 0, 0);
+  if (tid == 0) ctl.cand_n = 0u;
+  __syncthreads();
+  if (R.pen) {
+    uint32_t bad = 0;
+    for (int64_t h = h0 + tid; h < h1; h += kThreads) {
+      const int id = a.history_ids[h];
+      if (id < 0 || id >= V) {
+        bad = 1;
+        continue;
+      }
+      atomicOr(&sh.bitmap[id >> 5], 1u << (id & 31));
+    }
+    if (bad && status) atomicOr(status, NS_STATUS_BAD_HISTORY_ID);
+  }
+  if (tid == 0 && status && (in.src < 0 || in.src >= a.num_logit_rows)) atomicOr(status, NS_STATUS_BAD_SAMPLE_INDEX);
+  __syncthreads();
+
+  // row uniform
+  double u;
+  if (a.uniforms) {
+    u = (double)a.uniforms[row];
+  } else {
+    const uint64_t key = (P.flags & NS_ROW_SEED) ? P.seed : a.philox_seed;
+    u = philox_uniform(key, a.philox_offset, (uint64_t)(a.row_offset + row));
+  }
+  if (!(u >= 0.0)) u = 0.0;
+  if (u >= 1.0) u = 0x1.fffffffffffffp-1;
+
+  const Feed fd1 = feed_first<E>(ctl, i, ln);
+  // one ring pass of this row, specialised on whether the penalty is on
+  auto first_pass = [&](auto&& body) {
+    if (R.pen) ring_pass<E, true>(sh, ln, fd1, nch, stage, R.rp, pen_out, body);
+    else ring_pass<E, false>(sh, ln, fd1, nch, stage, R.rp, pen_out, body);
+  };
+
+  // ================================================================ first pass
+  Stats S;
+  float m0 = 0.0f;
+  uint32_t lumped = 0u;   // top-p: some e fell below the first locator level
+  float tau = -INFINITY;  // TOPK: bound on the k-th largest penalized logit
+  if (mode == kGreedy) {
+    float st = -INFINITY;
+    int sa = INT_MAX;
+    first_pass([&](int, const float(&x)[EPT], int idx0, bool live) {
+      if (!live) return;
+      float mv = x[0];
+#pragma unroll
+      for (int j = 1; j < EPT; ++j) mv = fmax_nan(mv, x[j]);
+      if (mv > st) {
+        int jj = 0;
+#pragma unroll
+        for (int j = EPT - 1; j >= 0; --j)
+          if (x[j] == mv) jj = j;
+        sa = idx0 + jj;
+      }
+      st = fmax_nan(st, mv);
+    });
+    S = block_stats(ctl, st, sa, 0.0, 0u, tid);
+  } else if (mode == kTopk) {
+    float tmax = -INFINITY;
+    int targ = INT_MAX;  // first argmax, for greedy rows with debug outputs
+    // each warp appends to its own list (slots counted in a warp-uniform register)
+    unsigned long long* wl = sh.cand + warp * kWarpCands;
+    int wcnt = 0;
+    const uint32_t lt = (1u << lane) - 1u;
+    first_pass([&](int c, const float(&x)[EPT], int idx0, bool live) {
+      float mv = x[0];
+#pragma unroll
+      for (int j = 1; j < EPT; ++j) mv = fmax_nan(mv, x[j]);
+      if (R.greedy && live && mv > tmax) {
+        int jj = 0;
+#pragma unroll
+        for (int j = EPT - 1; j >= 0; --j)
+          if (x[j] == mv) jj = j;
+        targ = idx0 + jj;
+      }
+      tmax = fmax_nan(tmax, mv);
+      if (c == 0 || c == kRefreshAt) tau = topk_bound(R, ctl, sh.tm, tmax, tid);
+      bool any = false;
+#pragma unroll
+      for (int j = 0; j < EPT; ++j) any |= (x[j] >= tau);
+      if (__any_sync(0xffffffffu, live && any)) {
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) {
+          const bool tk = live && (x[j] >= tau);
+          const uint32_t bal = __ballot_sync(0xffffffffu, tk);
+          if (tk) {
+            const int slot = wcnt + __popc(bal & lt);
+            if (slot < kWarpCands) wl[slot] = rank_key(scaled(R, x[j]), idx0 + j);
+          }
+          wcnt += __popc(bal);
+        }
+      }
+    });
+    if (lane == 0) ctl.red_j[warp] = wcnt;
+    S = block_stats(ctl, tmax, targ, 0.0, 0u, tid);
+    if (!(S.nan || S.mx == INFINITY || S.mx == -INFINITY)) tau = topk_bound(R, ctl, sh.tm, tmax, tid);
+  } else {
+    // GENERAL: e = exp(s - m0) with m0 the first chunk's maximum
+    float lmax = -INFINITY;
+    int larg = INT_MAX;
+    double lz = 0.0;
+    uint32_t over = 0u;
+    const bool with_e = R.k == 0;  // large top-k computes its masses after the select
+    first_pass([&](int c, const float(&x)[EPT], int idx0, bool live) {
+      float mv = x[0];
+#pragma unroll
+      for (int j = 1; j < EPT; ++j) mv = fmax_nan(mv, x[j]);
+      if (R.greedy && live && mv > lmax) {
+        int jj = 0;
+#pragma unroll
+        for (int j = EPT - 1; j >= 0; --j)
+          if (x[j] == mv) jj = j;
+        larg = idx0 + jj;
+      }
+      lmax = fmax_nan(lmax, mv);
+      if (!with_e) return;
+      if (c == 0) {
+        const bool nan = (lmax != lmax);
+        const uint32_t wk = __reduce_max_sync(0xffffffffu, nan ? 0u : f2key(lmax));
+        if (lane == 0) ctl.red_b[warp] = wk;
+        __syncthreads();
+        uint32_t ck = 0u;
+        for (int w = 0; w < kWarps; ++w) ck = max(ck, ctl.red_b[w]);
+        const float mx = key2f(ck);
+        m0 = (mx > -INFINITY && mx < INFINITY) ? scaled(R, mx) : 0.0f;
+      }
+      if (!live) return;
+      float s[EPT];
+      if (R.t_one) {
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) s[j] = x[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) s[j] = div_by_const(x[j], R.T, R.rT);
+      }
+      float part = 0.0f;
+#pragma unroll
+      for (int j = 0; j < EPT; ++j) {
+        const float e = exp_shifted(s[j], m0);
+        part = __fadd_rn(part, e);
+        if (want_hist) {
+          const uint32_t bits = __float_as_uint(e);
+          const uint32_t b = (kTopFine - bits) >> kShFine;
+          if (bits > kTopFine) over = 1u;  // e >= 2^32: the row maximum is far above m0
+          else if (b < (uint32_t)kBins) atomicAdd(&sh.hist[b], approx_mass13(bits));
+          else if (bits) lumped = 1u;      // 0 < e < 2^-32: below the level
+        }
+      }
+      lz += (double)part;
+    });
+    S = block_stats(ctl, lmax, larg, lz, over | (lumped << 1), tid);
+  }
+
+  // ================================================================ rows whose softmax is NaN
+  // NaN or +inf logits, or all -inf: uniform probabilities 1/V (sampler.py:76-80)
+  if (S.nan || S.mx == INFINITY || S.mx == -INFINITY) {
+    if (ring2) drain_pass(sh, ln, feed_second<E>(ctl, i, ln, false), nch, stage);
+    int tok;
+    if (R.greedy) {
+      // torch.argmax: the first NaN, else the first +inf, else index 0.  The
+      // penalty keeps NaN and +inf, so the raw logits decide.
+      int my_nan = INT_MAX, my_pinf = INT_MAX;
+      global_pass<E>(R, sh.bitmap, tid, [&](int, const float(&x)[EPT], int idx0, bool live) {
+        if (!live) return;
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) {
+          if (x[j] != x[j]) my_nan = min(my_nan, idx0 + j);
+          if (x[j] == INFINITY) my_pinf = min(my_pinf, idx0 + j);
+        }
+      });
+      my_nan = (int)__reduce_min_sync(0xffffffffu, (uint32_t)my_nan);
+      my_pinf = (int)__reduce_min_sync(0xffffffffu, (uint32_t)my_pinf);
+      if (lane == 0) {
+        ctl.red_i[warp] = my_nan;
+        ctl.red_j[warp] = my_pinf;
+      }
+      __syncthreads();
+      int fn = INT_MAX, fp = INT_MAX;
+      for (int w = 0; w < kWarps; ++w) {
+        fn = min(fn, ctl.red_i[w]);
+        fp = min(fp, ctl.red_j[w]);
+      }
+      tok = (fn != INT_MAX) ? fn : (fp != INT_MAX) ? fp : 0;
+    } else {
+      tok = min(V - 1, (int)(u * (double)V));
+    }
+    if (tid == 0) write_token(a.out_tokens, out_i32, row, tok);
+    if (debug) {
+      const float pu = 1.0f / (float)V;
+      global_pass<E>(R, sh.bitmap, tid, [&](int, const float(&x)[EPT], int idx0, bool live) {
+        if (!live) return;
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) {
+          if (a.out_probs) a.out_probs[out_off + idx0 + j] = pu;
+          if (a.out_filtered) a.out_filtered[out_off + idx0 + j] = scaled(R, x[j]);
+        }
+      });
+    }
+    return;
+  }
+
+  // ================================================================ GREEDY
+  if (mode == kGreedy) {
+    if (tid == 0) write_token(a.out_tokens, out_i32, row, S.arg);
+    return;
+  }
+
+  // ================================================================ TOPK
+  if (mode == kTopk) {
+    bool fits = true;
+    for (int w = 0; w < kWarps; ++w) fits &= ctl.red_j[w] <= kWarpCands;
+    if (fits) {
+      // the candidates at or above the final bound, from every warp's list
+      const float sig = scaled(R, tau);
+      unsigned long long* list = reinterpret_cast<unsigned long long*>(sh.hist);
+      if (tid == 0) ctl.list_n = 0u;
+      __syncthreads();
+      for (int r = tid; r < kCandCap; r += kThreads) {
+        const bool valid = (r % kWarpCands) < ctl.red_j[r / kWarpCands];
+        const unsigned long long key = valid ? sh.cand[r] : 0ull;
+        list_append(list, &ctl.list_n, valid && key_value(key) >= sig, key, kCandCap, lane);
+      }
+      __syncthreads();
+      const int nl = (int)ctl.list_n;
+      if (nl > 0) {
+        sort_keys(list, nl, tid);
+        if (warp == 0) {
+          // top-k keeps every rank whose value ties the k-th (sampler.py:53-58)
+          const float s0 = key_value(list[0]);
+          const float thr = key_value(list[min(R.k, nl) - 1]);
+          int n1 = nl;
+          for (int c0 = 0; c0 < nl; c0 += 32) {
+            const int r = c0 + lane;
+            const uint32_t below = __ballot_sync(0xffffffffu, r < nl && key_value(list[r]) < thr);
+            if (below) {
+              n1 = c0 + __ffs(below) - 1;
+              break;
+            }
+          }
+          float* ce = reinterpret_cast<float*>(sh.cand);  // masses by rank (the candidates are consumed)
+          double z = 0.0;
+          for (int r = lane; r < n1; r += 32) {
+            const float e = exp_shifted(key_value(list[r]), s0);
+            ce[r] = e;
+            z += (double)e;
+          }
+          z = warp_dsum(z);
+          __syncwarp();
+          int m2 = n1;
+          if (R.topp) {
+            // keep exactly ranks 0..j0 in (value desc, index asc) order (sampler.py:60-73)
+            double run = 0.0;
+            int j0 = -1;
+            for (int c0 = 0; c0 < n1 && j0 < 0; c0 += 32) {
+              const int r = c0 + lane;
+              const double inc = warp_incl_f64(r < n1 ? (double)ce[r] : 0.0, lane) + run;
+              const uint32_t bal = __ballot_sync(0xffffffffu, r < n1 && topp_crossed(inc, z, R.p));
+              if (bal) j0 = c0 + __ffs(bal) - 1;
+              run = __shfl_sync(0xffffffffu, inc, 31);
+            }
+            if (j0 >= 0) m2 = j0 + 1;
+            z = 0.0;
+            for (int r = lane; r < m2; r += 32) z += (double)ce[r];
+            z = warp_dsum(z);
+          }
+          // inverse CDF in vocabulary order over the kept ranks
+          const double target = u * z;
+          int tok = INT_MAX, last = -1;
+          for (int r = lane; r < m2; r += 32) {
+            const int ir = key_index(list[r]);
+            const double er = (double)ce[r];
+            if (er > 0.0) last = max(last, ir);
+            double before = 0.0;
+            for (int q2 = 0; q2 < m2; ++q2)
+              if (key_index(list[q2]) < ir) before += (double)ce[q2];
+            if (er > 0.0 && before <= target && target < before + er) tok = min(tok, ir);
+          }
+          tok = (int)__reduce_min_sync(0xffffffffu, (uint32_t)tok);
+          last = (int)__reduce_max_sync(0xffffffffu, (uint32_t)(last + 1)) - 1;
+          if (tok == INT_MAX) tok = last >= 0 ? last : key_index(list[0]);  // rounding at the very top
+          if (R.greedy) tok = key_index(list[0]);
+          if (lane == 0) {
+            write_token(a.out_tokens, out_i32, row, tok);
+            ctl.dec_thr = key_value(list[m2 - 1]);
+            ctl.dec_thr_idx = key_index(list[m2 - 1]);
+            ctl.dec_z = z;
+          }
+        }
+        if (debug) {
+          __syncthreads();
+          const float s0 = key_value(list[0]);
+          const float thr2 = ctl.dec_thr;
+          const int thr_idx2 = ctl.dec_thr_idx;
+          const double z2 = ctl.dec_z;
+          global_pass<E>(R, sh.bitmap, tid, [&](int, const float(&x)[EPT], int idx0, bool live) {
+            if (!live) return;
+#pragma unroll
+            for (int j = 0; j < EPT; ++j) {
+              const float s = scaled(R, x[j]);
+              const bool kept = s > thr2 || (s == thr2 && idx0 + j <= thr_idx2);
+              if (a.out_filtered) a.out_filtered[out_off + idx0 + j] = kept ? s : -INFINITY;
+              if (a.out_probs)
+                a.out_probs[out_off + idx0 + j] = kept ? (float)((double)exp_shifted(s, s0) / z2) : 0.0f;
+            }
+          });
+        }
+        return;
+      }
+    }
+    // a warp's candidate list overflowed: the row takes the general path
+    if (tid == 0 && status) atomicOr(status, NS_STATUS_CAP_OVERFLOW);
+    mode = kGeneral;
+  }
+
+  // ================================================================ GENERAL
+  const float m = scaled(R, S.mx);
+  Keep K;
+  K.m0 = m0;
+  K.have_k = false;
+  K.thr_k = -INFINITY;
+  K.window = false;
+  K.win_lo = K.win_hi = 0u;
+  K.thr = -INFINITY;
+  K.thr_idx = INT_MAX;
+  double z = S.z;
+  // the first pass's masses hold unless top-k comes first or e passed 2^32
+  const bool first_ok = R.k == 0 && !S.over;
+  if (R.k > 0) {
+    K.have_k = true;
+    K.thr_k = scaled(R, radix_select<E>(R, sh, tid));
+  }
+  // (Re)compute the masses against m0 with a re-read of the row, plus the
+  // locator histogram of level `lv` for top-p rows.
+  auto stats_pass = [&](const Level& lv, bool hist_only) {
+    const Keep K0 = K;
+    if (R.topp)
+      for (int b = tid; b < kBins / 4; b += kThreads) reinterpret_cast<uint4*>(sh.hist)[b] = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+    double lz = 0.0;
+    uint32_t lump = 0u;
+    const bool hist = R.topp;
+    global_pass<E>(R, sh.bitmap, tid, [&](int, const float(&x)[EPT], int, bool live) {
+      if (!live) return;
+      float part = 0.0f;
+#pragma unroll
+      for (int j = 0; j < EPT; ++j) {
+        const float e = K0.mass(scaled(R, x[j]));
+        part = __fadd_rn(part, e);
+        if (hist) {
+          const uint32_t bits = __float_as_uint(e);
+          const uint32_t b = (lv.top - bits) >> lv.sh;
+          if (bits <= lv.top && b < (uint32_t)kBins) atomicAdd(&sh.hist[b], approx_mass13(bits));
+          else if (bits) lump = 1u;
+        }
+      }
+      lz += (double)part;
+    });
+    lumped = __syncthreads_or((int)lump) ? 1u : 0u;
+    if (!hist_only) z = block_segments(ctl, lz, tid);
+  };
+  Level lv{kTopFine, kShFine};
+  lumped = S.lumped ? 1u : 0u;
+  if (!first_ok) {
+    m0 = m;
+    K.m0 = m0;
+    stats_pass(lv, false);
+  }
+
+  double zk = z;
+  bool ring_used = false;
+  if (R.topp) {
+    topp_window(ctl, sh.hist, lv, 0.0, z, R.p, tid);
+    if (!ctl.sel_found && lumped) {
+      // the boundary may lie among masses below the level: locate it on the wide one
+      lv = Level{kTopWide, kShWide};
+      stats_pass(lv, true);
+      topp_window(ctl, sh.hist, lv, 0.0, z, R.p, tid);
+    }
+    const bool crossed = ctl.sel_found != 0;
+    uint32_t win_lo = 0u, win_hi = 0u;
+    float est = 0.0f;
+    if (crossed) {
+      win_lo = lv.lo_key(ctl.sel_hi);
+      win_hi = lv.hi_key(ctl.sel_lo);
+      est = ctl.sel_est;
+    }
+    int refines = 0;
+    bool force_refine = false;
+    while (crossed) {
+      if ((est > 0.9f * (float)kCandCap || force_refine) && lv.sh > 0 && refines < 3) {
+        // ---- refine inside [win_lo, win_hi]: finer buckets, exact mass above the window
+        const uint32_t span = win_hi - win_lo + 1u;
+        int sh2 = 0;
+        while (((span + (1u << sh2) - 1u) >> sh2) > (uint32_t)(kBins - 1)) ++sh2;
+        if (sh2 >= lv.sh) {
+          refines = 3;  // the window is too wide to split further: collect it as it is
+          continue;
+        }
+        force_refine = false;
+        ++refines;
+        for (int b = tid; b < kBins / 4; b += kThreads) reinterpret_cast<uint4*>(sh.hist)[b] = make_uint4(0, 0, 0, 0);
+        __syncthreads();
+        double la = 0.0;
+        const Keep K1 = K;
+        const uint32_t wlo = max(win_lo, 1u), whi = win_hi;
+        global_pass<E>(R, sh.bitmap, tid, [&](int, const float(&x)[EPT], int, bool live) {
+          if (!live) return;
+          float part = 0.0f;
+#pragma unroll
+          for (int j = 0; j < EPT; ++j) {
+            const float e = K1.mass(scaled(R, x[j]));
+            const uint32_t bits = __float_as_uint(e);
+            if (bits > whi) part = __fadd_rn(part, e);
+            else if (bits >= wlo) atomicAdd(&sh.hist[(whi - bits) >> sh2], approx_mass13(bits));
+          }
+          la += (double)part;
+        });
+        const double above_lv = block_dsum(ctl, la, tid);
+        const Level lv2{win_hi, sh2};
+        topp_window(ctl, sh.hist, lv2, above_lv, z, R.p, tid);
+        if (ctl.sel_found) {
+          lv = lv2;
+          win_lo = lv.lo_key(ctl.sel_hi);
+          win_hi = lv.hi_key(ctl.sel_lo);
+          est = ctl.sel_est;
+        } else {
+          refines = 3;  // keep the previous window: it still contains the boundary
+        }
+        continue;
+      }
+      // ---- collection: exact mass above the window per warp range; window members
+      if (tid == 0) ctl.cand_n = 0u;
+      __syncthreads();
+      double la = 0.0;
+      const Keep K1 = K;
+      const uint32_t wlo = max(win_lo, 1u), whi = win_hi;
+      auto collect = [&](int, const float(&x)[EPT], int idx0, bool live) {
+        if (!live) return;
+        float s[EPT];
+        if (R.t_one) {
+#pragma unroll
+          for (int j = 0; j < EPT; ++j) s[j] = x[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < EPT; ++j) s[j] = div_by_const(x[j], R.T, R.rT);
+        }
+        float part = 0.0f;
+        bool anym = false;
+        uint32_t bits[EPT];
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) {
+          const float e = K1.mass(s[j]);
+          bits[j] = __float_as_uint(e);
+          if (bits[j] > whi) part = __fadd_rn(part, e);
+          anym |= (bits[j] >= wlo && bits[j] <= whi);
+        }
+        la += (double)part;
+        if (anym) {
+          // rare: append this thread's window members one by one
+#pragma unroll
+          for (int j = 0; j < EPT; ++j) {
+            if (bits[j] >= wlo && bits[j] <= whi) {
+              const uint32_t slot = atomicAdd(&ctl.cand_n, 1u);
+              if (slot < (uint32_t)kCandCap) sh.cand[slot] = rank_key(s[j], idx0 + j);
+            }
+          }
+        }
+      };
+      if (ring2 && !ring_used) {
+        ring_used = true;
+        const Feed fd2 = feed_second<E>(ctl, i, ln, true);
+        if (R.pen) ring_pass<E, true>(sh, ln, fd2, nch, stage, R.rp, nullptr, collect);
+        else ring_pass<E, false>(sh, ln, fd2, nch, stage, R.rp, nullptr, collect);
+      } else {
+        global_pass<E>(R, sh.bitmap, tid, collect);
+      }
+      const double above = block_segments(ctl, la, tid);
+      const uint32_t ntot = ctl.cand_n;
+      if (ntot > (uint32_t)kCandCap && lv.sh > 0 && refines < 3) {
+        force_refine = true;  // the window held more elements than estimated
+        continue;
+      }
+      // ---- decision on the sorted window members: the first rank whose
+      // inclusive mass crosses (block-wide scan, 4 ranks per thread)
+      const int n = (int)min(ntot, (uint32_t)kCandCap);
+      if (ntot > (uint32_t)kCandCap && tid == 0 && status) atomicOr(status, NS_STATUS_CAP_OVERFLOW);
+      sort_keys(sh.cand, n, tid);
+      if (tid == 0) ctl.misc = INT_MAX;
+      float er[4];
+      double tsum = 0.0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int r = 4 * tid + q;
+        er[q] = r < n ? exp_shifted(key_value(sh.cand[r]), m0) : 0.0f;
+        tsum += (double)er[q];
+      }
+      {
+        const double inc = warp_incl_f64(tsum, lane);
+        if (lane == 31) ctl.red_e[warp] = inc;
+        __syncthreads();
+        double run = above + inc - tsum;
+        for (int w = 0; w < warp; ++w) run += ctl.red_e[w];
+        if (ntot <= (uint32_t)kCandCap) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            run += (double)er[q];
+            if (er[q] > 0.0f && topp_crossed(run, z, R.p)) {
+              atomicMin(&ctl.misc, 4 * tid + q);
+              break;
+            }
+          }
+        }
+        __syncthreads();
+      }
+      // no crossing inside (or overflow): keep the whole window
+      const int j0 = ctl.misc == INT_MAX ? n - 1 : ctl.misc;
+      if (tid == 0) {
+        ctl.dec_thr = n > 0 ? key_value(sh.cand[j0]) : -INFINITY;
+        ctl.dec_thr_idx = n > 0 ? key_index(sh.cand[j0]) : INT_MAX;
+      }
+      // kept members join their warp ranges' masses
+      double lk = 0.0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int r = 4 * tid + q;
+        if (r <= j0 && er[q] > 0.0f) {
+          atomicAdd(&ctl.seg[key_index(sh.cand[r]) / W], (double)er[q]);
+          lk += (double)er[q];
+        }
+      }
+      zk = above + block_dsum(ctl, lk, tid);  // (its barriers order the range updates)
+      K.window = true;
+      K.win_lo = win_lo;
+      K.win_hi = win_hi;
+      K.thr = ctl.dec_thr;
+      K.thr_idx = ctl.dec_thr_idx;
+      break;
+    }
+    if (!crossed) {
+      // top-p never crosses: every element stays; draw over all masses
+      double lz = 0.0;
+      const Keep K1 = K;
+      auto plain = [&](int, const float(&x)[EPT], int, bool live) {
+        if (!live) return;
+        float part = 0.0f;
+#pragma unroll
+        for (int j = 0; j < EPT; ++j) part = __fadd_rn(part, K1.mass(scaled(R, x[j])));
+        lz += (double)part;
+      };
+      if (ring2 && !ring_used) {
+        ring_used = true;
+        const Feed fd2 = feed_second<E>(ctl, i, ln, true);
+        if (R.pen) ring_pass<E, true>(sh, ln, fd2, nch, stage, R.rp, nullptr, plain);
+        else ring_pass<E, false>(sh, ln, fd2, nch, stage, R.rp, nullptr, plain);
+      } else {
+        global_pass<E>(R, sh.bitmap, tid, plain);
+      }
+      zk = block_segments(ctl, lz, tid);
+    }
+  }
+  if (ring2 && !ring_used) drain_pass(sh, ln, feed_second<E>(ctl, i, ln, false), nch, stage);
+
+  // ---- the draw
+  const int tok = R.greedy ? S.arg : draw_token<E>(R, sh, K, u * zk, S.arg, tid);
+  if (tid == 0) write_token(a.out_tokens, out_i32, row, tok == INT_MAX ? 0 : tok);
+  if (debug) {
+    global_pass<E>(R, sh.bitmap, tid, [&](int, const float(&x)[EPT], int idx0, bool live) {
+      if (!live) return;
+#pragma unroll
+      for (int j = 0; j < EPT; ++j) {
+        const float s = scaled(R, x[j]);
+        const float e = K.mass(s);
+        const bool kept = K.kept(s, e, idx0 + j);
+        if (a.out_filtered) a.out_filtered[out_off + idx0 + j] = kept ? s : -INFINITY;
+        if (a.out_probs) a.out_probs[out_off + idx0 + j] = (kept && e > 0.f) ? (float)((double)e / zk) : 0.0f;
+      }
+    });
+  }
+}
+
+// ---------------------------------------------------------------- the kernel
+template <class E>
+__global__ void __launch_bounds__(kThreads, 2) row_kernel(const NsSampleArgs a, int W, int nch) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const Layout L = make_layout(a.vocab_size);
+  Sh sh;
+  sh.ctl = reinterpret_cast<Ctl*>(smem + L.ctl);
+  sh.ring = smem + L.ring;
+  sh.bitmap = reinterpret_cast<uint32_t*>(smem + L.bitmap);
+  sh.cand = reinterpret_cast<unsigned long long*>(smem + L.cand);
+  sh.hist = reinterpret_cast<uint32_t*>(smem + L.hist);
+  sh.tm = reinterpret_cast<uint32_t*>(smem + L.tm);
+  Ctl& ctl = *sh.ctl;
+  const int tid = threadIdx.x;
+  const int G = gridDim.x;
+  const int row0 = blockIdx.x;
+  const bool debug = (a.out_filtered != nullptr) || (a.out_probs != nullptr);
+  const Lane ln = make_lane<E>(a.vocab_size, W, tid);
+
+  if (row0 < a.num_rows) fetch_row_inputs(a, ctl.rin[0], row0, tid);
+  if (row0 + G < a.num_rows) fetch_row_inputs(a, ctl.rin[1], row0 + G, tid);
+  __syncthreads();
+  if (tid == 0) make_plan(a, ctl, 0, row0, debug);
+  __syncthreads();
+  ring_start<E>(ctl, sh.ring, ln);
+  int stage = 0;
+  for (int i = 0, row = row0; row < a.num_rows; ++i, row += G) {
+    __syncthreads();  // the previous row is finished; row i+1's inputs are in place
+    if (tid == 0) make_plan(a, ctl, i + 1, row + G, debug);
+    if (row + 2 * G < a.num_rows) fetch_row_inputs(a, ctl.rin[(i + 2) & 3], row + 2 * G, tid);
+    sample_row<E>(a, sh, ln, stage, i, row, nch, W);
+  }
+  cp_async_wait_all();  // nothing may land in shared memory after the block exits
+}
+
+// ---------------------------------------------------------------- host side
+struct DevState {
+  size_t smem_set[2] = {0, 0};
+  int blocks_per_sm[2] = {0, 0};
+  size_t occ_for[2] = {0, 0};
+  int sms = 0;
+};
+std::mutex g_mu;
+DevState g_dev[64];
+
+}  // namespace rk
+
+bool rows_supported(const NsSampleArgs& a) {
+  const int esize = a.logits_dtype == NS_DTYPE_BF16 ? 2 : 4;
+  const uintptr_t p = reinterpret_cast<uintptr_t>(a.logits);
+  return a.vocab_size >= rk::kMinVocab && a.vocab_size <= rk::kMaxVocab && p % 16 == 0 &&
+         ((int64_t)a.logits_row_stride * esize) % 16 == 0 && ((int64_t)a.vocab_size * esize) % 16 == 0;
+}
+
+int rows_launch(const NsSampleArgs& a, cudaStream_t stream, int device, std::string& err) {
+  using namespace rk;
+  const bool bf16 = a.logits_dtype == NS_DTYPE_BF16;
+  const int ept = bf16 ? EBF16::kEPT : EF32::kEPT;
+  // warp range: V / 16 rounded up to whole 16-byte slots
+  const int W = ((a.vocab_size + kWarps - 1) / kWarps + ept - 1) / ept * ept;
+  const int nch = (W + 32 * ept - 1) / (32 * ept);
+  const Layout L = make_layout(a.vocab_size);
+  const void* fn = bf16 ? reinterpret_cast<const void*>(&row_kernel<EBF16>)
+                        : reinterpret_cast<const void*>(&row_kernel<EF32>);
+  const int fi = bf16 ? 1 : 0;
+  int per_sm = 0, sms = 0;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (device < 0 || device >= 64) {
+      err = "ns_sample: device ordinal >= 64";
+      return NS_ERR_UNSUPPORTED;
+    }
+    DevState& ds = g_dev[device];
+    cudaError_t e;
+    if (ds.sms == 0) {
+      e = cudaDeviceGetAttribute(&ds.sms, cudaDevAttrMultiProcessorCount, device);
+      if (e != cudaSuccess) {
+        err = std::string("cudaDeviceGetAttribute: ") + cudaGetErrorString(e);
+        return NS_ERR_CUDA;
+      }
+    }
+    if (ds.smem_set[fi] < L.total) {
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+      if (e != cudaSuccess) {
+        err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+        return NS_ERR_CUDA;
+      }
+      ds.smem_set[fi] = L.total;
+    }
+    if (ds.occ_for[fi] != L.total) {
+      int n = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kThreads, L.total);
+      if (e != cudaSuccess || n <= 0) {
+        err = std::string("cudaOccupancyMaxActiveBlocksPerMultiprocessor: ") +
+              (e != cudaSuccess ? cudaGetErrorString(e) : "no block fits");
+        return NS_ERR_CUDA;
+      }
+      ds.blocks_per_sm[fi] = n;
+      ds.occ_for[fi] = L.total;
+    }
+    per_sm = ds.blocks_per_sm[fi];
+    sms = ds.sms;
+  }
+  const int cap = per_sm * sms;
+  const int grid = a.num_rows < cap ? a.num_rows : cap;
+  void* args[] = {const_cast<NsSampleArgs*>(&a), const_cast<int*>(&W), const_cast<int*>(&nch)};
+  const cudaError_t e = cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kThreads), args, L.total, stream);
+  if (e != cudaSuccess) {
+    err = std::string("row kernel launch: ") + cudaGetErrorString(e);
+    return NS_ERR_CUDA;
+  }
+  return NS_OK;
+}
+
+}  // namespace ns

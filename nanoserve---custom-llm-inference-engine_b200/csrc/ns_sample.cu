@@ -41,12 +41,14 @@
 
 #include <climits>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
 
 #include "../../include/nanoserve_sampler.h"
 #include "ns_device.cuh"
+#include "ns_rows.h"
 
 namespace ns {
 
@@ -153,43 +155,6 @@ __host__ __device__ inline Layout make_layout(int W) {
   L.total = o;
   return L;
 }
-
-// ---------------------------------------------------------------- warp helpers
-__device__ __forceinline__ double warp_dsum(double v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ uint32_t warp_incl_u32(uint32_t v, int lane) {
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    uint32_t t = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v += t;
-  }
-  return v;
-}
-__device__ __forceinline__ double warp_incl_f64(double v, int lane) {
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    double t = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v += t;
-  }
-  return v;
-}
-
-// The reference keeps sorted rank j of the top-p pass iff j == 0 or
-// float32(cum[j-1]) <= top_p (sampler.py:66-70); the first rank whose
-// inclusive mass passes this test is the last one kept.
-__device__ __forceinline__ bool topp_crossed(double cum, double z, float p) {
-  return (float)(cum / z) > p;
-}
-
-// Sort key: ascending keys give (value descending, index ascending).
-__device__ __forceinline__ unsigned long long rank_key(float s, int idx) {
-  return ((unsigned long long)(~f2key(s)) << 32) | (uint32_t)idx;
-}
-__device__ __forceinline__ float key_value(unsigned long long k) { return key2f(~(uint32_t)(k >> 32)); }
-__device__ __forceinline__ int key_index(unsigned long long k) { return (int)(uint32_t)k; }
 
 // Bitonic sort of keys[0, n) ascending in place (n <= kCap), by the whole CTA.
 // Entries [n, pow2) are filled with the largest key.
@@ -383,10 +348,6 @@ __device__ float lower_preimage(const Row& R, float b) {
   return -INFINITY;
 }
 
-__device__ __forceinline__ void write_token(void* out, bool i32, int row, int tok) {
-  if (i32) reinterpret_cast<int32_t*>(out)[row] = tok;
-  else reinterpret_cast<int64_t*>(out)[row] = tok;
-}
 
 // Block-wide exclusive scan of one u32 per thread (thread 0 first).
 __device__ uint32_t block_excl_u32(Ctl& ctl, uint32_t v, uint32_t& total, int tid) {
@@ -1543,6 +1504,17 @@ struct DeviceState {
 std::mutex g_mu;
 DeviceState g_dev[64];
 
+// Batches of at least this many rows use the one-block-per-row kernel.
+constexpr int kRowsMinBatch = 32;
+
+enum class SamplePath { kAuto, kCluster, kRows };
+SamplePath sample_path() {
+  const char* e = std::getenv("NS_SAMPLE_PATH");
+  if (e && std::strcmp(e, "cluster") == 0) return SamplePath::kCluster;
+  if (e && std::strcmp(e, "rows") == 0) return SamplePath::kRows;
+  return SamplePath::kAuto;
+}
+
 int slice_width(int V) {
   const int W = (V + kCluster - 1) / kCluster;
   return (W + 7) & ~7;
@@ -1594,9 +1566,19 @@ int ns_sample(const NsSampleArgs* args, void* stream) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return fail(NS_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(err));
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+
+  // Kernel choice: one block per row once the batch is large enough, the
+  // cluster kernel otherwise.  NS_SAMPLE_PATH=cluster|rows forces one of them
+  // (rows only where its layout conditions hold).
+  const SamplePath path = sample_path();
+  if (rows_supported(a) && (path == SamplePath::kRows || (path == SamplePath::kAuto && a.num_rows >= kRowsMinBatch))) {
+    std::string msg;
+    const int rc = rows_launch(a, st, dev, msg);
+    return rc == NS_OK ? NS_OK : fail(rc, msg);
+  }
   const int W = slice_width(a.vocab_size);
   const Layout L = make_layout(W);
-  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(kThreads, 1, 1);

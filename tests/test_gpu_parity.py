@@ -20,6 +20,13 @@ pytestmark = pytest.mark.gpu
 W = importlib.import_module(H.PKG + ".workloads")
 
 
+@pytest.fixture(params=["cluster", "rows"], autouse=True)
+def sample_path(request, monkeypatch):
+    """Run every test through both kernels (rows only where its layout holds)."""
+    monkeypatch.setenv("NS_SAMPLE_PATH", request.param)
+    return request.param
+
+
 def _check(rep: H.Report):
     assert not rep.failures, "\n".join(rep.failures)
 
@@ -63,9 +70,10 @@ def test_full_decode_batch_tokens():
     _check(H.compare(dbg, w.logits, w.params, w.histories, w.uniforms))
 
 
-def test_edge_cases():
+@pytest.mark.parametrize("V", [4096, 32768])
+def test_edge_cases(V):
     dev = _dev()
-    case = C.edge_case()
+    case = C.edge_case(V)
     lg = torch.from_numpy(case.logits).to(dev)
     gpu = H.run_cabi(lg, case.params, case.histories, case.uniforms)
     _check(H.compare(gpu, case.logits, case.params, case.histories, case.uniforms))
@@ -161,3 +169,36 @@ def test_host_side_errors_are_reported():
     a.num_rows = 3
     with pytest.raises(H.cabi.NsError, match="required"):
         H.cabi.ns_sample(a, 0)
+
+
+def test_fallback_paths():
+    """Rows that leave the single-pass fast paths: candidate overflow on ties,
+    a maximum far above the first chunk's, wide and deep top-p windows."""
+    dev = _dev()
+    V = 32768
+    rng = np.random.default_rng(21)
+    SP = importlib.import_module(H.PKG + ".config").SamplingParams
+    rows, params, hists = [], [], []
+
+    def add(x, p, h=()):
+        rows.append(np.asarray(x, dtype=np.float32))
+        params.append(p)
+        hists.append(list(h))
+
+    base = lambda: (rng.standard_normal(V) * 2.0).astype(np.float32)  # noqa: E731
+    add(np.full(V, 1.5), SP(temperature=1.0, top_k=50))                       # all tied: top-k overflow
+    add(np.linspace(-5, 5, V), SP(temperature=1.0, top_k=64))                 # ascending: bound rises late
+    x = base(); x[V - 3] = 200.0; add(x, SP(temperature=1.0, top_p=0.9))      # max far above chunk 0
+    x = base(); x[V - 3] = 200.0; add(x, SP(temperature=1.0))                 # same, plain sampling
+    add(base() * np.float32(0.1), SP(temperature=1.0, top_p=0.999))          # flat: big window
+    add(base(), SP(temperature=1.0, top_p=0.9999))                            # boundary deep in the tail
+    add(np.round(base() * 4) / 4, SP(temperature=1.0, top_p=0.7))            # many exact ties
+    add(base(), SP(temperature=0.25, top_k=300, top_p=0.95, repetition_penalty=1.3),
+        rng.integers(0, V, 500).tolist())                                     # large top-k + penalty
+    add(base(), SP(temperature=0.0, top_k=40, top_p=0.5))                     # greedy with filters
+    x = base(); x[:8192] = -np.inf; add(x, SP(temperature=1.0, top_p=0.8))    # first chunks all -inf
+    x = base() * np.float32(30.0); add(x, SP(temperature=1.0, top_p=0.95))    # masses below 2^-32
+    lg = torch.from_numpy(np.stack(rows)).to(dev)
+    u = np.random.default_rng(5).random(len(rows)).astype(np.float32)
+    gpu = H.run_cabi(lg, params, hists, u)
+    _check(H.compare(gpu, np.stack(rows), params, hists, u))

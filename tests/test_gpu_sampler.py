@@ -14,6 +14,13 @@ NS = importlib.import_module(H.PKG)
 W = importlib.import_module(H.PKG + ".workloads")
 
 
+@pytest.fixture(params=["cluster", "rows"], autouse=True)
+def sample_path(request, monkeypatch):
+    """Run every test through both kernels (rows only where its layout holds)."""
+    monkeypatch.setenv("NS_SAMPLE_PATH", request.param)
+    return request.param
+
+
 def _dev():
     assert torch.cuda.is_available(), "GPU test run without a CUDA device"
     return torch.device("cuda:0")
