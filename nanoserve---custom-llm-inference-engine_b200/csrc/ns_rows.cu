@@ -259,13 +259,13 @@ __device__ __forceinline__ float scaled(const RowCtx& R, float x) {
 
 // Smallest float c <= b with RN(c/T) == RN(b/T): the lower end of the set of
 // logits whose scaled value is at least RN(b/T).
-__device__ __noinline__ float lower_preimage(const RowCtx& R, float b) {
-  if (R.t_one || !(b > -INFINITY) || !(b < INFINITY)) return b;
-  const float target = div_by_const(b, R.T, R.rT);
+__device__ __noinline__ float lower_preimage(float b, bool t_one, float T, float rT) {
+  if (t_one || !(b > -INFINITY) || !(b < INFINITY)) return b;
+  const float target = div_by_const(b, T, rT);
   float c = b;
   for (int i = 0; i < 64; ++i) {
     const float d = nextafterf(c, -INFINITY);
-    if (div_by_const(d, R.T, R.rT) == target) c = d; else return c;
+    if (div_by_const(d, T, rT) == target) c = d; else return c;
   }
   return -INFINITY;
 }
@@ -387,13 +387,15 @@ __device__ __forceinline__ void ring_pass(const Sh& sh, const Lane& ln, const Fe
   }
 }
 
-// Consume a second pass nobody needs without fetching it.
-__device__ __noinline__ void drain_pass(const Sh& sh, const Lane& ln, const Feed& fd, int nch, int& stage) {
+// Consume a second pass nobody needs without fetching it; returns the new
+// ring stage.  (Out of line, so everything is passed by value.)
+__device__ __noinline__ int drain_pass(unsigned char* ring, Feed fd, Lane ln, int nch, int stage) {
   for (int c = 0; c < nch; ++c) {
     cp_async_wait_ring();
-    ring_refill(fd, sh.ring, stage, c, nch, ln);
+    ring_refill(fd, ring, stage, c, nch, ln);
     stage = stage + 1 == kStages ? 0 : stage + 1;
   }
+  return stage;
 }
 
 // Calls f(c, x, idx0, live) for every chunk c of the row with this thread's
@@ -448,7 +450,7 @@ __device__ __forceinline__ void fetch_row_inputs(const NsSampleArgs& a, RowIn& d
 }
 
 // Plan of this block's i-th row (global row `row`), from its fetched inputs.
-__device__ void make_plan(const NsSampleArgs& a, Ctl& ctl, int i, int row, bool debug) {
+__device__ __forceinline__ void make_plan(const NsSampleArgs& a, Ctl& ctl, int i, int row, bool debug) {
   RowPlan& pl = ctl.plan[i & 1];
   if (row >= a.num_rows) {
     pl.valid = 0;
@@ -466,7 +468,7 @@ __device__ void make_plan(const NsSampleArgs& a, Ctl& ctl, int i, int row, bool 
 
 // ---------------------------------------------------------------- block reductions
 // Block-wide exclusive scan of one u32 per thread (thread 0 first).
-__device__ uint32_t block_excl_u32(Ctl& ctl, uint32_t v, uint32_t& total, int tid) {
+__device__ __forceinline__ uint32_t block_excl_u32(Ctl& ctl, uint32_t v, uint32_t& total, int tid) {
   const int lane = tid & 31, warp = tid >> 5;
   const uint32_t inc = warp_incl_u32(v, lane);
   if (lane == 31) ctl.red_u[warp] = inc;
@@ -482,7 +484,7 @@ __device__ uint32_t block_excl_u32(Ctl& ctl, uint32_t v, uint32_t& total, int ti
   return wpre + inc - v;
 }
 
-__device__ double block_dsum(Ctl& ctl, double v, int tid) {
+__device__ __forceinline__ double block_dsum(Ctl& ctl, double v, int tid) {
   const double w = warp_dsum(v);
   if ((tid & 31) == 0) ctl.red_e[tid >> 5] = w;
   __syncthreads();
@@ -493,7 +495,7 @@ __device__ double block_dsum(Ctl& ctl, double v, int tid) {
 }
 
 // Per-warp-range totals of per-thread masses into ctl.seg, and their sum.
-__device__ double block_segments(Ctl& ctl, double v, int tid) {
+__device__ __forceinline__ double block_segments(Ctl& ctl, double v, int tid) {
   const double w = warp_dsum(v);
   if ((tid & 31) == 0) ctl.seg[tid >> 5] = w;
   __syncthreads();
@@ -515,7 +517,7 @@ struct Stats {
   bool over;
   bool lumped;
 };
-__device__ Stats block_stats(Ctl& ctl, float v, int arg, double z, uint32_t flags, int tid) {
+__device__ __forceinline__ Stats block_stats(Ctl& ctl, float v, int arg, double z, uint32_t flags, int tid) {
   const int lane = tid & 31, warp = tid >> 5;
   const bool nan = (v != v);
   const uint32_t k = nan ? 0u : f2key(v);
@@ -556,20 +558,84 @@ __device__ Stats block_stats(Ctl& ctl, float v, int arg, double z, uint32_t flag
   return S;
 }
 
-// Bitonic sort of keys[0, n) ascending in place (n <= kCandCap), whole block.
-__device__ void bitonic_sort(unsigned long long* keys, int n, int tid) {
-  int np = 1;
+// Bitonic sorting of up to kCandCap 64-bit keys.  Every stage with stride
+// below 128 runs inside one warp on a 128-key segment held in registers
+// (element i = base + 32 r + lane), so only strides >= 128 need the block.
+__device__ __forceinline__ void cmpx_regs(unsigned long long& a, unsigned long long& b, bool up) {
+  const bool sw = (a > b) == up;
+  const unsigned long long t = a;
+  a = sw ? b : a;
+  b = sw ? t : b;
+}
+__device__ __forceinline__ void cmpx_lanes(unsigned long long& v, int j, bool up, int lane) {
+  const unsigned long long o = __shfl_xor_sync(0xffffffffu, v, j);
+  const bool lower = (lane & j) == 0;
+  v = (lower == up) ? (v < o ? v : o) : (v < o ? o : v);
+}
+// Stages j = 64 .. 1 of bitonic level k on one segment.
+__device__ __forceinline__ void seg_merge(unsigned long long (&v)[4], int base, int lane, int k) {
+  bool up[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) up[r] = ((base + 32 * r + lane) & k) == 0;
+  cmpx_regs(v[0], v[2], up[0]);
+  cmpx_regs(v[1], v[3], up[1]);
+  cmpx_regs(v[0], v[1], up[0]);
+  cmpx_regs(v[2], v[3], up[2]);
+#pragma unroll
+  for (int j = 16; j > 0; j >>= 1) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) cmpx_lanes(v[r], j, up[r], lane);
+  }
+}
+// Levels k = 2 .. 128 on one segment (ascending or descending by bit 128 of base).
+__device__ __forceinline__ void seg_sort(unsigned long long (&v)[4], int base, int lane) {
+#pragma unroll
+  for (int k = 2; k <= 128; k <<= 1) {
+    bool up[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) up[r] = ((base + 32 * r + lane) & k) == 0;
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j == 64) {
+        cmpx_regs(v[0], v[2], up[0]);
+        cmpx_regs(v[1], v[3], up[1]);
+      } else if (j == 32) {
+        cmpx_regs(v[0], v[1], up[0]);
+        cmpx_regs(v[2], v[3], up[2]);
+      } else {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) cmpx_lanes(v[r], j, up[r], lane);
+      }
+    }
+  }
+}
+
+// Sort keys[0, n) ascending in place (n <= kCandCap; the buffer holds
+// kCandCap keys).  Whole block; ends with a barrier.
+__device__ __noinline__ void sort_keys(unsigned long long* keys, int n, int tid) {
+  const int lane = tid & 31, warp = tid >> 5;
+  int np = 128;
   while (np < n) np <<= 1;
   for (int i = n + tid; i < np; i += kThreads) keys[i] = ~0ull;
   __syncthreads();
-  for (int k = 2; k <= np; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
+  const int nseg = np >> 7;
+  unsigned long long v[4];
+  if (warp < nseg) {
+    const int base = warp << 7;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) v[r] = keys[base + 32 * r + lane];
+    seg_sort(v, base, lane);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) keys[base + 32 * r + lane] = v[r];
+  }
+  __syncthreads();
+  for (int k = 256; k <= np; k <<= 1) {
+    for (int j = k >> 1; j >= 128; j >>= 1) {
       for (int i = tid; i < np; i += kThreads) {
         const int l = i ^ j;
         if (l > i) {
           const unsigned long long a = keys[i], b = keys[l];
-          const bool up = (i & k) == 0;
-          if ((a > b) == up) {
+          if ((a > b) == ((i & k) == 0)) {
             keys[i] = b;
             keys[l] = a;
           }
@@ -577,66 +643,15 @@ __device__ void bitonic_sort(unsigned long long* keys, int n, int tid) {
       }
       __syncthreads();
     }
-  }
-}
-
-// Sort keys[0, n) ascending (n <= 32 * NPL) with one warp, in registers
-// (bitonic network; element i lives in lane i % 32, register i / 32).
-template <int NPL>
-__device__ __forceinline__ void warp_sort(unsigned long long* keys, int n, int lane) {
-  unsigned long long v[NPL];
+    if (warp < nseg) {
+      const int base = warp << 7;
 #pragma unroll
-  for (int r = 0; r < NPL; ++r) {
-    const int i = r * 32 + lane;
-    v[r] = i < n ? keys[i] : ~0ull;
-  }
+      for (int r = 0; r < 4; ++r) v[r] = keys[base + 32 * r + lane];
+      seg_merge(v, base, lane, k);
 #pragma unroll
-  for (int k = 2; k <= 32 * NPL; k <<= 1) {
-#pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      if (j >= 32) {
-        const int jr = j >> 5;
-#pragma unroll
-        for (int r = 0; r < NPL; ++r) {
-          if ((r & jr) == 0) {
-            const int r2 = r | jr;
-            const bool up = ((r * 32 + lane) & k) == 0;
-            const unsigned long long a = v[r], b = v[r2];
-            const bool sw = (a > b) == up;
-            v[r] = sw ? b : a;
-            v[r2] = sw ? a : b;
-          }
-        }
-      } else {
-#pragma unroll
-        for (int r = 0; r < NPL; ++r) {
-          const unsigned long long o = __shfl_xor_sync(0xffffffffu, v[r], j);
-          const bool up = ((r * 32 + lane) & k) == 0;
-          const bool lower = (lane & j) == 0;
-          const unsigned long long mn = v[r] < o ? v[r] : o, mx = v[r] < o ? o : v[r];
-          v[r] = (lower == up) ? mn : mx;
-        }
-      }
+      for (int r = 0; r < 4; ++r) keys[base + 32 * r + lane] = v[r];
     }
-  }
-#pragma unroll
-  for (int r = 0; r < NPL; ++r) {
-    const int i = r * 32 + lane;
-    if (i < n) keys[i] = v[r];
-  }
-}
-
-// Sort keys[0, n) ascending: one warp in registers for short lists, the
-// whole block otherwise.  Whole block; ends with a barrier.
-__device__ void sort_keys(unsigned long long* keys, int n, int tid) {
-  if (n <= 128) {
-    if (tid < 32) warp_sort<4>(keys, n, tid);
     __syncthreads();
-  } else if (n <= 256) {
-    if (tid < 32) warp_sort<8>(keys, n, tid);
-    __syncthreads();
-  } else {
-    bitonic_sort(keys, n, tid);
   }
 }
 
@@ -662,7 +677,9 @@ __device__ __forceinline__ void list_append(unsigned long long* list, uint32_t* 
 // down to its quarter binade and extended to every logit whose scaled value
 // ties with it: a lower bound for the k-th largest scaled logit of the row.
 // Whole block.
-__device__ __noinline__ float topk_bound(const RowCtx& R, Ctl& ctl, uint32_t* tm, float tmax, int tid) {
+__device__ __noinline__ float topk_bound(int topk, bool t_one, float T, float rT, Ctl* ctlp, uint32_t* tm, float tmax,
+                                         int tid) {
+  Ctl& ctl = *ctlp;
   for (int b = tid; b < kTmBins; b += kThreads) tm[b] = 0u;
   __syncthreads();
   if (tid == 0) ctl.misc = -1;
@@ -679,7 +696,7 @@ __device__ __noinline__ float topk_bound(const RowCtx& R, Ctl& ctl, uint32_t* tm
   }
   uint32_t tot;
   const uint32_t pre = block_excl_u32(ctl, s, tot, tid);
-  const uint32_t k = (uint32_t)R.k;
+  const uint32_t k = (uint32_t)topk;
   if (pre < k && pre + s >= k) {
     uint32_t run = pre;
 #pragma unroll
@@ -695,14 +712,14 @@ __device__ __noinline__ float topk_bound(const RowCtx& R, Ctl& ctl, uint32_t* tm
   const int b = ctl.misc;
   const uint32_t bkey = b < 0 ? 0u : (uint32_t)b << kTmShift;
   const float bound = (b < 0 || bkey < 0x00800000u) ? -INFINITY : key2f(bkey);
-  return lower_preimage(R, bound);
+  return lower_preimage(bound, t_one, T, rT);
 }
 
 // ---------------------------------------------------------------- radix select
 // k-th largest penalized logit by a 3-level radix select over its key
 // (11/11/10 bits), re-reading the row three times.  Whole block.
 template <class E>
-__device__ float radix_select(const RowCtx& R, const Sh& sh, int tid) {
+__device__ __noinline__ float radix_select(const RowCtx R, const Sh sh, int tid) {
   Ctl& ctl = *sh.ctl;
   uint32_t* h = sh.hist;
   uint32_t prefix = 0u, krem = (uint32_t)R.k;
@@ -762,8 +779,9 @@ __device__ float radix_select(const RowCtx& R, const Sh& sh, int tid) {
 // crossing, given that each bucket's approximate mass is within a factor
 // (1 - 2^-12) of its exact mass, plus an estimate of its element count.
 // `base` is the exact mass above the level's range, `z` the row total.
-__device__ __noinline__ void topp_window(Ctl& ctl, const uint32_t* h, const Level& lv, double base, double z,
+__device__ __noinline__ void topp_window(Ctl* ctlp, const uint32_t* h, const Level lv, double base, double z,
                                          float p, int tid) {
+  Ctl& ctl = *ctlp;
   const int lane = tid & 31, warp = tid >> 5;
   {
     // coarse sums: 8 threads per coarse bucket, 8 fine buckets each
@@ -890,7 +908,7 @@ __device__ __forceinline__ void kept_masses(const RowCtx& R, const uint32_t* bit
 // element, walked by warp 0.  Falls back to the last kept element when
 // rounding leaves the target past the total, then to `fallback`.
 template <class E>
-__device__ __noinline__ int draw_token(const RowCtx& R, const Sh& sh, const Keep& K, double target, int fallback,
+__device__ __noinline__ int draw_token(const RowCtx R, const Sh sh, const Keep K, double target, int fallback,
                                        int tid) {
   constexpr int kPer = (kMaxChunks + kWarps - 1) / kWarps;  // pieces per warp at most
   Ctl& ctl = *sh.ctl;
@@ -1129,7 +1147,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
         targ = idx0 + jj;
       }
       tmax = fmax_nan(tmax, mv);
-      if (c == 0 || c == kRefreshAt) tau = topk_bound(R, ctl, sh.tm, tmax, tid);
+      if (c == 0 || c == kRefreshAt) tau = topk_bound(R.k, R.t_one, R.T, R.rT, &ctl, sh.tm, tmax, tid);
       bool any = false;
 #pragma unroll
       for (int j = 0; j < EPT; ++j) any |= (x[j] >= tau);
@@ -1148,7 +1166,8 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
     });
     if (lane == 0) ctl.red_j[warp] = wcnt;
     S = block_stats(ctl, tmax, targ, 0.0, 0u, tid);
-    if (!(S.nan || S.mx == INFINITY || S.mx == -INFINITY)) tau = topk_bound(R, ctl, sh.tm, tmax, tid);
+    if (!(S.nan || S.mx == INFINITY || S.mx == -INFINITY))
+      tau = topk_bound(R.k, R.t_one, R.T, R.rT, &ctl, sh.tm, tmax, tid);
   } else {
     // GENERAL: e = exp(s - m0) with m0 the first chunk's maximum
     float lmax = -INFINITY;
@@ -1209,7 +1228,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
   // ================================================================ rows whose softmax is NaN
   // NaN or +inf logits, or all -inf: uniform probabilities 1/V (sampler.py:76-80)
   if (S.nan || S.mx == INFINITY || S.mx == -INFINITY) {
-    if (ring2) drain_pass(sh, ln, feed_second<E>(ctl, i, ln, false), nch, stage);
+    if (ring2) stage = drain_pass(sh.ring, feed_second<E>(ctl, i, ln, false), ln, nch, stage);
     int tok;
     if (R.greedy) {
       // torch.argmax: the first NaN, else the first +inf, else index 0.  The
@@ -1424,12 +1443,12 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
   double zk = z;
   bool ring_used = false;
   if (R.topp) {
-    topp_window(ctl, sh.hist, lv, 0.0, z, R.p, tid);
+    topp_window(&ctl, sh.hist, lv, 0.0, z, R.p, tid);
     if (!ctl.sel_found && lumped) {
       // the boundary may lie among masses below the level: locate it on the wide one
       lv = Level{kTopWide, kShWide};
       stats_pass(lv, true);
-      topp_window(ctl, sh.hist, lv, 0.0, z, R.p, tid);
+      topp_window(&ctl, sh.hist, lv, 0.0, z, R.p, tid);
     }
     const bool crossed = ctl.sel_found != 0;
     uint32_t win_lo = 0u, win_hi = 0u;
@@ -1472,7 +1491,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
         });
         const double above_lv = block_dsum(ctl, la, tid);
         const Level lv2{win_hi, sh2};
-        topp_window(ctl, sh.hist, lv2, above_lv, z, R.p, tid);
+        topp_window(&ctl, sh.hist, lv2, above_lv, z, R.p, tid);
         if (ctl.sel_found) {
           lv = lv2;
           win_lo = lv.lo_key(ctl.sel_hi);
@@ -1613,7 +1632,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       zk = block_segments(ctl, lz, tid);
     }
   }
-  if (ring2 && !ring_used) drain_pass(sh, ln, feed_second<E>(ctl, i, ln, false), nch, stage);
+  if (ring2 && !ring_used) stage = drain_pass(sh.ring, feed_second<E>(ctl, i, ln, false), ln, nch, stage);
 
   // ---- the draw
   const int tok = R.greedy ? S.arg : draw_token<E>(R, sh, K, u * zk, S.arg, tid);
