@@ -84,11 +84,17 @@ constexpr int kMaxChunks = (kMaxVocab / kWarps + 127) / 128;  // pieces per warp
 // ---------------------------------------------------------------- element formats
 // 16 bytes of a row as logits.
 struct EF32 {
+  static constexpr uint32_t kNegInf2 = 0xFF800000u;  // a 32-bit word of -inf logits
   static constexpr int kEPT = 4;            // elements per thread per chunk
   static constexpr int kPiece = 32 * kEPT;  // elements per warp piece
   using Raw = float4;
   static __device__ __forceinline__ Raw zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
   static __device__ __forceinline__ Raw lds(const unsigned char* p) { return *reinterpret_cast<const float4*>(p); }
+  static __device__ __forceinline__ Raw lds_s(uint32_t a) {
+    Raw r;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "r"(a));
+    return r;
+  }
   static __device__ __forceinline__ Raw ldg(const char* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
   static __device__ __forceinline__ void unpack(const Raw& r, float (&x)[kEPT]) {
     x[0] = r.x;
@@ -98,11 +104,17 @@ struct EF32 {
   }
 };
 struct EBF16 {
+  static constexpr uint32_t kNegInf2 = 0xFF80FF80u;
   static constexpr int kEPT = 8;
   static constexpr int kPiece = 32 * kEPT;
   using Raw = uint4;
   static __device__ __forceinline__ Raw zero() { return make_uint4(0u, 0u, 0u, 0u); }
   static __device__ __forceinline__ Raw lds(const unsigned char* p) { return *reinterpret_cast<const uint4*>(p); }
+  static __device__ __forceinline__ Raw lds_s(uint32_t a) {
+    Raw r;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
+    return r;
+  }
   static __device__ __forceinline__ Raw ldg(const char* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
   // bf16 -> fp32 is exact: the bf16 bits are the high half of the fp32 bits
   static __device__ __forceinline__ void unpack(const Raw& r, float (&x)[kEPT]) {
@@ -273,9 +285,9 @@ __device__ __noinline__ float lower_preimage(float b, bool t_one, float T, float
 // The thread's 16 bytes of a row as penalized logits (sampler.py:31-38).
 template <class E, bool PEN>
 __device__ __forceinline__ void penalized(const uint32_t* bitmap, float rp, const typename E::Raw& raw, int idx0,
-                                          float (&x)[E::kEPT]) {
+                                          float (&x)[E::kEPT], bool live = true) {
   E::unpack(raw, x);
-  if (PEN) {
+  if (PEN && live) {
     const uint32_t m = (bitmap[idx0 >> 5] >> (idx0 & 31)) & ((1u << E::kEPT) - 1u);
     if (m) {
 #pragma unroll
@@ -302,21 +314,6 @@ __device__ __forceinline__ void cp_async_wait_ring() {
 
 __device__ __forceinline__ unsigned char* stage_slot(unsigned char* ring, int stage, int tid) {
   return ring + stage * kChunkBytes + tid * 16;
-}
-
-// The stage at `stage` held chunk c of the current pass; refill this
-// thread's slot of it kStages chunks further on and commit the group (empty
-// when there is nothing to fetch).
-__device__ __forceinline__ void ring_refill(const Feed& f, unsigned char* ring, int stage, int c, int nch,
-                                            const Lane& ln) {
-  c += kStages;
-  const char* src = f.cur;
-  if (c >= nch) {
-    c -= nch;
-    src = f.after;
-  }
-  if (src != nullptr && c < ln.nv) cp_async16(stage_slot(ring, stage, ln.tid), src + c * kPieceBytes);
-  cp_async_commit();
 }
 
 // This thread's bytes of row `src` (16-byte aligned: the host admits only
@@ -353,49 +350,81 @@ __device__ __forceinline__ void ring_start(const Ctl& ctl, unsigned char* ring, 
   const RowPlan& pl = ctl.plan[0];
   const char* src = lane_src<E>(pl.src, ln);
   for (int c = 0; c < kStages; ++c) {
-    if (pl.valid && c < ln.nv) cp_async16(stage_slot(ring, c, ln.tid), src + c * kPieceBytes);
+    unsigned char* dst = stage_slot(ring, c, ln.tid);
+    if (pl.valid && c < ln.nv) cp_async16(dst, src + c * kPieceBytes);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(E::kNegInf2, E::kNegInf2, E::kNegInf2, E::kNegInf2);
     cp_async_commit();
   }
 }
 
+__device__ __forceinline__ void cp_async16_s(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// This thread's walk through the ring during one pass: the shared address of
+// its slot in the stage it reads next, and where its refills (kStages chunks
+// ahead) come from -- a running pointer with a count of refills left from
+// the current source, switched to `after` when the refills leave the pass.
+struct RingWalk {
+  uint32_t slot, ring_lo, ring_hi;
+  const char* gp;
+  int left;
+  __device__ __forceinline__ RingWalk(const Sh& sh, const Lane& ln, const Feed& fd, int stage) {
+    ring_lo = smem_addr(sh.ring) + ln.tid * 16;
+    ring_hi = ring_lo + kStages * kChunkBytes;
+    slot = ring_lo + stage * kChunkBytes;
+    gp = fd.cur + kStages * kPieceBytes;
+    left = fd.cur ? ln.nv - kStages : 0;
+  }
+  // refill the slot just read with chunk c + kStages (one commit group); a
+  // slot this lane has no data for is filled with -inf logits instead
+  __device__ __forceinline__ void refill(const Feed& fd, const Lane& ln, int c, int nch, uint32_t pad) {
+    if (c == nch - kStages) {
+      gp = fd.after;
+      left = fd.after ? ln.nv : 0;
+    }
+    if (left > 0) cp_async16_s(slot, gp);
+    else asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(slot), "r"(pad) : "memory");
+    gp += kPieceBytes;
+    --left;
+    cp_async_commit();
+    slot += kChunkBytes;
+    if (slot == ring_hi) slot = ring_lo;
+  }
+};
+
 // One pass of the current row through the ring: body(c, x, idx0, live) for
-// every chunk c with this thread's penalized logits; the penalized values are
-// also written to pen_out when given.
+// every chunk c with this thread's penalized logits (-inf where the lane has
+// no element: live false).
 template <class E, bool PEN, class F>
 __device__ __forceinline__ void ring_pass(const Sh& sh, const Lane& ln, const Feed& fd, int nch, int& stage, float rp,
-                                          float* pen_out, F&& body) {
+                                          F&& body) {
   constexpr int EPT = E::kEPT;
-  for (int c = 0; c < nch; ++c) {
+  RingWalk rw(sh, ln, fd, stage);
+  int idx0 = ln.base;
+  for (int c = 0; c < nch; ++c, idx0 += E::kPiece) {
     cp_async_wait_ring();
+    const typename E::Raw raw = E::lds_s(rw.slot);
+    rw.refill(fd, ln, c, nch, E::kNegInf2);
     const bool live = c < ln.nv;
-    const typename E::Raw raw = live ? E::lds(stage_slot(sh.ring, stage, ln.tid)) : E::zero();
-    ring_refill(fd, sh.ring, stage, c, nch, ln);
-    stage = stage + 1 == kStages ? 0 : stage + 1;
-    const int idx0 = ln.base + c * E::kPiece;
     float x[EPT];
-    if (live) {
-      penalized<E, PEN>(sh.bitmap, rp, raw, idx0, x);
-      if (pen_out) {
-#pragma unroll
-        for (int j = 0; j < EPT; ++j) pen_out[idx0 + j] = x[j];
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < EPT; ++j) x[j] = -INFINITY;
-    }
+    penalized<E, PEN>(sh.bitmap, rp, raw, idx0, x, live);
     body(c, x, idx0, live);
   }
+  stage = (stage + nch) % kStages;
 }
 
 // Consume a second pass nobody needs without fetching it; returns the new
 // ring stage.  (Out of line, so everything is passed by value.)
-__device__ __noinline__ int drain_pass(unsigned char* ring, Feed fd, Lane ln, int nch, int stage) {
+__device__ __noinline__ int drain_pass(unsigned char* ring, Feed fd, Lane ln, int nch, int stage, uint32_t pad) {
+  Sh sh;
+  sh.ring = ring;
+  RingWalk rw(sh, ln, fd, stage);
   for (int c = 0; c < nch; ++c) {
     cp_async_wait_ring();
-    ring_refill(fd, ring, stage, c, nch, ln);
-    stage = stage + 1 == kStages ? 0 : stage + 1;
+    rw.refill(fd, ln, c, nch, pad);
   }
-  return stage;
+  return (stage + nch) % kStages;
 }
 
 // Calls f(c, x, idx0, live) for every chunk c of the row with this thread's
@@ -1030,6 +1059,23 @@ __device__ __noinline__ int draw_token(const RowCtx R, const Sh sh, const Keep K
   return ctl.token;
 }
 
+// The first index at which this thread holds `best`, which it first saw in
+// chunk `bc` (re-read from global memory); INT_MAX when it saw none.
+template <class E>
+__device__ __forceinline__ int arg_of(const RowCtx& R, const uint32_t* bitmap, const Lane& ln, float best, int bc) {
+  if (bc < 0) return INT_MAX;
+  const int idx0 = ln.base + bc * E::kPiece;
+  const typename E::Raw raw = E::ldg(lane_src<E>(R.src, ln) + bc * kPieceBytes);
+  float x[E::kEPT];
+  if (R.pen) penalized<E, true>(bitmap, R.rp, raw, idx0, x);
+  else penalized<E, false>(bitmap, R.rp, raw, idx0, x);
+  int jj = E::kEPT - 1;
+#pragma unroll
+  for (int j = E::kEPT - 1; j >= 0; --j)
+    if (x[j] == best) jj = j;
+  return idx0 + jj;
+}
+
 // ---------------------------------------------------------------- one row
 template <class E>
 __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, const Lane& ln, int& stage, int i,
@@ -1061,7 +1107,6 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
   R.pen = (P.flags & NS_ROW_PENALTY) != 0u && a.history_offsets && h1 > h0;
   const bool ring2 = ctl.plan[i & 1].passes == 2;
   int mode = row_mode(P, V, debug);
-  float* const pen_out = a.out_penalized ? a.out_penalized + (int64_t)row * V : nullptr;
   const int64_t out_off = (int64_t)row * V;
 
   // ---------------- setup: penalty bitmap, histograms, counters
@@ -1101,8 +1146,8 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
   const Feed fd1 = feed_first<E>(ctl, i, ln);
   // one ring pass of this row, specialised on whether the penalty is on
   auto first_pass = [&](auto&& body) {
-    if (R.pen) ring_pass<E, true>(sh, ln, fd1, nch, stage, R.rp, pen_out, body);
-    else ring_pass<E, false>(sh, ln, fd1, nch, stage, R.rp, pen_out, body);
+    if (R.pen) ring_pass<E, true>(sh, ln, fd1, nch, stage, R.rp, body);
+    else ring_pass<E, false>(sh, ln, fd1, nch, stage, R.rp, body);
   };
 
   // ================================================================ first pass
@@ -1110,27 +1155,25 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
   float m0 = 0.0f;
   uint32_t lumped = 0u;   // top-p: some e fell below the first locator level
   float tau = -INFINITY;  // TOPK: bound on the k-th largest penalized logit
+  // argmax bookkeeping for greedy rows: the largest value and the chunk it
+  // was first seen in; the element index is recovered after the pass
+  float best = -INFINITY;
+  int best_c = -1;
   if (mode == kGreedy) {
     float st = -INFINITY;
-    int sa = INT_MAX;
-    first_pass([&](int, const float(&x)[EPT], int idx0, bool live) {
-      if (!live) return;
+    first_pass([&](int c, const float(&x)[EPT], int, bool) {
       float mv = x[0];
 #pragma unroll
       for (int j = 1; j < EPT; ++j) mv = fmax_nan(mv, x[j]);
-      if (mv > st) {
-        int jj = 0;
-#pragma unroll
-        for (int j = EPT - 1; j >= 0; --j)
-          if (x[j] == mv) jj = j;
-        sa = idx0 + jj;
+      if (mv > best) {
+        best = mv;
+        best_c = c;
       }
       st = fmax_nan(st, mv);
     });
-    S = block_stats(ctl, st, sa, 0.0, 0u, tid);
+    S = block_stats(ctl, st, arg_of<E>(R, sh.bitmap, ln, best, best_c), 0.0, 0u, tid);
   } else if (mode == kTopk) {
     float tmax = -INFINITY;
-    int targ = INT_MAX;  // first argmax, for greedy rows with debug outputs
     // each warp appends to its own list (slots counted in a warp-uniform register)
     unsigned long long* wl = sh.cand + warp * kWarpCands;
     int wcnt = 0;
@@ -1139,19 +1182,13 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       float mv = x[0];
 #pragma unroll
       for (int j = 1; j < EPT; ++j) mv = fmax_nan(mv, x[j]);
-      if (R.greedy && live && mv > tmax) {
-        int jj = 0;
-#pragma unroll
-        for (int j = EPT - 1; j >= 0; --j)
-          if (x[j] == mv) jj = j;
-        targ = idx0 + jj;
+      if (R.greedy && mv > best) {
+        best = mv;
+        best_c = c;
       }
       tmax = fmax_nan(tmax, mv);
       if (c == 0 || c == kRefreshAt) tau = topk_bound(R.k, R.t_one, R.T, R.rT, &ctl, sh.tm, tmax, tid);
-      bool any = false;
-#pragma unroll
-      for (int j = 0; j < EPT; ++j) any |= (x[j] >= tau);
-      if (__any_sync(0xffffffffu, live && any)) {
+      if (__any_sync(0xffffffffu, live && mv >= tau)) {
 #pragma unroll
         for (int j = 0; j < EPT; ++j) {
           const bool tk = live && (x[j] >= tau);
@@ -1165,13 +1202,12 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       }
     });
     if (lane == 0) ctl.red_j[warp] = wcnt;
-    S = block_stats(ctl, tmax, targ, 0.0, 0u, tid);
+    S = block_stats(ctl, tmax, R.greedy ? arg_of<E>(R, sh.bitmap, ln, best, best_c) : INT_MAX, 0.0, 0u, tid);
     if (!(S.nan || S.mx == INFINITY || S.mx == -INFINITY))
       tau = topk_bound(R.k, R.t_one, R.T, R.rT, &ctl, sh.tm, tmax, tid);
   } else {
     // GENERAL: e = exp(s - m0) with m0 the first chunk's maximum
     float lmax = -INFINITY;
-    int larg = INT_MAX;
     double lz = 0.0;
     uint32_t over = 0u;
     const bool with_e = R.k == 0;  // large top-k computes its masses after the select
@@ -1179,12 +1215,9 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       float mv = x[0];
 #pragma unroll
       for (int j = 1; j < EPT; ++j) mv = fmax_nan(mv, x[j]);
-      if (R.greedy && live && mv > lmax) {
-        int jj = 0;
-#pragma unroll
-        for (int j = EPT - 1; j >= 0; --j)
-          if (x[j] == mv) jj = j;
-        larg = idx0 + jj;
+      if (R.greedy && mv > best) {
+        best = mv;
+        best_c = c;
       }
       lmax = fmax_nan(lmax, mv);
       if (!with_e) return;
@@ -1222,13 +1255,24 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       }
       lz += (double)part;
     });
-    S = block_stats(ctl, lmax, larg, lz, over | (lumped << 1), tid);
+    S = block_stats(ctl, lmax, R.greedy ? arg_of<E>(R, sh.bitmap, ln, best, best_c) : INT_MAX, lz,
+                    over | (lumped << 1), tid);
+  }
+
+  if (a.out_penalized) {
+    // debug output: the logits after the repetition penalty (sampler.py:31-38)
+    float* const pen_out = a.out_penalized + out_off;
+    global_pass<E>(R, sh.bitmap, tid, [&](int, const float(&x)[EPT], int idx0, bool live) {
+      if (!live) return;
+#pragma unroll
+      for (int j = 0; j < EPT; ++j) pen_out[idx0 + j] = x[j];
+    });
   }
 
   // ================================================================ rows whose softmax is NaN
   // NaN or +inf logits, or all -inf: uniform probabilities 1/V (sampler.py:76-80)
   if (S.nan || S.mx == INFINITY || S.mx == -INFINITY) {
-    if (ring2) stage = drain_pass(sh.ring, feed_second<E>(ctl, i, ln, false), ln, nch, stage);
+    if (ring2) stage = drain_pass(sh.ring, feed_second<E>(ctl, i, ln, false), ln, nch, stage, E::kNegInf2);
     int tok;
     if (R.greedy) {
       // torch.argmax: the first NaN, else the first +inf, else index 0.  The
@@ -1543,8 +1587,8 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       if (ring2 && !ring_used) {
         ring_used = true;
         const Feed fd2 = feed_second<E>(ctl, i, ln, true);
-        if (R.pen) ring_pass<E, true>(sh, ln, fd2, nch, stage, R.rp, nullptr, collect);
-        else ring_pass<E, false>(sh, ln, fd2, nch, stage, R.rp, nullptr, collect);
+        if (R.pen) ring_pass<E, true>(sh, ln, fd2, nch, stage, R.rp, collect);
+        else ring_pass<E, false>(sh, ln, fd2, nch, stage, R.rp, collect);
       } else {
         global_pass<E>(R, sh.bitmap, tid, collect);
       }
@@ -1624,15 +1668,15 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       if (ring2 && !ring_used) {
         ring_used = true;
         const Feed fd2 = feed_second<E>(ctl, i, ln, true);
-        if (R.pen) ring_pass<E, true>(sh, ln, fd2, nch, stage, R.rp, nullptr, plain);
-        else ring_pass<E, false>(sh, ln, fd2, nch, stage, R.rp, nullptr, plain);
+        if (R.pen) ring_pass<E, true>(sh, ln, fd2, nch, stage, R.rp, plain);
+        else ring_pass<E, false>(sh, ln, fd2, nch, stage, R.rp, plain);
       } else {
         global_pass<E>(R, sh.bitmap, tid, plain);
       }
       zk = block_segments(ctl, lz, tid);
     }
   }
-  if (ring2 && !ring_used) stage = drain_pass(sh.ring, feed_second<E>(ctl, i, ln, false), ln, nch, stage);
+  if (ring2 && !ring_used) stage = drain_pass(sh.ring, feed_second<E>(ctl, i, ln, false), ln, nch, stage, E::kNegInf2);
 
   // ---- the draw
   const int tok = R.greedy ? S.arg : draw_token<E>(R, sh, K, u * zk, S.arg, tid);
