@@ -137,17 +137,20 @@ __device__ __forceinline__ uint32_t approx_mass13(uint32_t bits) { return ((bits
 
 // Bucket b of a locator level covers bits of e in [top - (b+1)*2^sh + 1,
 // top - b*2^sh]; top + 1 is a multiple of 2^sh, so each bucket lies inside
-// one binade.
+// one binade.  Masses are added without a range test: indices past the last
+// bucket are clamped into it, and where that happens (lump_last) its mass is
+// left out of the search.
 struct Level {
   uint32_t top;
   int sh;
+  bool lump_last;  // the last bucket also holds everything below the level: its mass is unknown
   __device__ __forceinline__ uint32_t lo_key(int b) const {
     const uint64_t span = (uint64_t)(b + 1) << sh;
     return span > (uint64_t)top + 1u ? 0u : top - (uint32_t)span + 1u;
   }
   __device__ __forceinline__ uint32_t hi_key(int b) const { return top - ((uint32_t)b << sh); }
   __device__ __forceinline__ double mass(uint32_t sum13, int b) const {
-    if (sum13 == 0u) return 0.0;
+    if (sum13 == 0u || (lump_last && b == kBins - 1)) return 0.0;
     // sum13 * 2^(exponent - 139), the power of two built from its bits
     const int ex = (int)(lo_key(b) >> 23) - 139 + 1023;
     return (double)sum13 * __longlong_as_double((long long)ex << 52);
@@ -397,12 +400,11 @@ struct RingWalk {
 // every chunk c with this thread's penalized logits (-inf where the lane has
 // no element: live false).
 template <class E, bool PEN, class F>
-__device__ __forceinline__ void ring_pass(const Sh& sh, const Lane& ln, const Feed& fd, int nch, int& stage, float rp,
-                                          F&& body) {
+__device__ __forceinline__ void ring_range(const Sh& sh, const Lane& ln, const Feed& fd, RingWalk& rw, int c0, int c1,
+                                           int nch, float rp, F&& body) {
   constexpr int EPT = E::kEPT;
-  RingWalk rw(sh, ln, fd, stage);
-  int idx0 = ln.base;
-  for (int c = 0; c < nch; ++c, idx0 += E::kPiece) {
+  int idx0 = ln.base + c0 * E::kPiece;
+  for (int c = c0; c < c1; ++c, idx0 += E::kPiece) {
     cp_async_wait_ring();
     const typename E::Raw raw = E::lds_s(rw.slot);
     rw.refill(fd, ln, c, nch, E::kNegInf2);
@@ -411,7 +413,28 @@ __device__ __forceinline__ void ring_pass(const Sh& sh, const Lane& ln, const Fe
     penalized<E, PEN>(sh.bitmap, rp, raw, idx0, x, live);
     body(c, x, idx0, live);
   }
+}
+template <class E, bool PEN, class F>
+__device__ __forceinline__ void ring_pass(const Sh& sh, const Lane& ln, const Feed& fd, int nch, int& stage, float rp,
+                                          F&& body) {
+  RingWalk rw(sh, ln, fd, stage);
+  ring_range<E, PEN>(sh, ln, fd, rw, 0, nch, nch, rp, body);
   stage = (stage + nch) % kStages;
+}
+
+// Maximum of this thread's penalized logits in the pass's first chunk, read
+// ahead of the pass (which then finds the chunk already landed).
+template <class E>
+__device__ __forceinline__ float peek_max(const Sh& sh, const Lane& ln, int stage, bool pen, float rp) {
+  cp_async_wait_ring();
+  const typename E::Raw raw = E::lds_s(smem_addr(sh.ring) + stage * kChunkBytes + ln.tid * 16);
+  float x[E::kEPT];
+  if (pen) penalized<E, true>(sh.bitmap, rp, raw, ln.base, x, ln.nv > 0);
+  else penalized<E, false>(sh.bitmap, rp, raw, ln.base, x);
+  float mv = x[0];
+#pragma unroll
+  for (int j = 1; j < E::kEPT; ++j) mv = fmax_nan(mv, x[j]);
+  return mv;
 }
 
 // Consume a second pass nobody needs without fetching it; returns the new
@@ -702,19 +725,10 @@ __device__ __forceinline__ void list_append(unsigned long long* list, uint32_t* 
 }
 
 // ---------------------------------------------------------------- top-k bound
-// The k-th largest per-thread maximum (a logit before temperature), rounded
-// down to its quarter binade and extended to every logit whose scaled value
-// ties with it: a lower bound for the k-th largest scaled logit of the row.
-// Whole block.
-__device__ __noinline__ float topk_bound(int topk, bool t_one, float T, float rT, Ctl* ctlp, uint32_t* tm, float tmax,
-                                         int tid) {
-  Ctl& ctl = *ctlp;
-  for (int b = tid; b < kTmBins; b += kThreads) tm[b] = 0u;
-  __syncthreads();
-  if (tid == 0) ctl.misc = -1;
-  if (tmax == tmax) atomicAdd(&tm[f2key(tmax) >> kTmShift], 1u);
-  __syncthreads();
-  // thread t owns buckets [kTmBins - 4(t+1), kTmBins - 4t), scanned from the top
+// Over the kTmBins-bucket count histogram `tm` (bucket kTmBins - 1 holds the
+// largest keys): the bucket where the count from the top reaches `need`, and
+// the count above it.  Whole block; thread t scans buckets from the top.
+__device__ __forceinline__ int tm_crossing(Ctl& ctl, const uint32_t* tm, uint32_t need, uint32_t& above, int tid) {
   uint32_t cnt[4];
   uint32_t s = 0;
   const int bhi = kTmBins - 1 - 4 * tid;
@@ -725,22 +739,49 @@ __device__ __noinline__ float topk_bound(int topk, bool t_one, float T, float rT
   }
   uint32_t tot;
   const uint32_t pre = block_excl_u32(ctl, s, tot, tid);
-  const uint32_t k = (uint32_t)topk;
-  if (pre < k && pre + s >= k) {
+  if (pre < need && pre + s >= need) {
     uint32_t run = pre;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      run += cnt[j];
-      if (run >= k) {
+      if (run + cnt[j] >= need) {
         ctl.misc = bhi - j;
+        ctl.sel_before = run;
         break;
       }
+      run += cnt[j];
     }
   }
   __syncthreads();
-  const int b = ctl.misc;
-  const uint32_t bkey = b < 0 ? 0u : (uint32_t)b << kTmShift;
-  const float bound = (b < 0 || bkey < 0x00800000u) ? -INFINITY : key2f(bkey);
+  above = ctl.sel_before;
+  return ctl.misc;
+}
+
+// The k-th largest per-thread maximum (a logit before temperature), rounded
+// down to 2^10 units of its order key (two histogram levels) and extended to
+// every logit whose scaled value ties with it: a lower bound for the k-th
+// largest scaled logit of the row.  Whole block.
+__device__ __noinline__ float topk_bound(int topk, bool t_one, float T, float rT, Ctl* ctlp, uint32_t* tm, float tmax,
+                                         int tid) {
+  Ctl& ctl = *ctlp;
+  const uint32_t key = (tmax == tmax) ? f2key(tmax) : 0u;  // NaN maxima take no part
+  for (int b = tid; b < kTmBins; b += kThreads) tm[b] = 0u;
+  __syncthreads();
+  if (tid == 0) ctl.misc = -1;
+  if (key) atomicAdd(&tm[key >> kTmShift], 1u);
+  __syncthreads();
+  uint32_t above;
+  const int b1 = tm_crossing(ctl, tm, (uint32_t)topk, above, tid);
+  if (b1 < 0) return -INFINITY;  // fewer maxima than k
+  // second level inside bucket b1: bits 20..10 of the key
+  for (int b = tid; b < kTmBins; b += kThreads) tm[b] = 0u;
+  __syncthreads();
+  if (tid == 0) ctl.misc = -1;
+  if (key && (int)(key >> kTmShift) == b1) atomicAdd(&tm[(key >> 10) & (kTmBins - 1)], 1u);
+  __syncthreads();
+  uint32_t above2;
+  const int b2 = tm_crossing(ctl, tm, (uint32_t)topk - above, above2, tid);
+  const uint32_t bkey = ((uint32_t)b1 << kTmShift) | ((uint32_t)max(b2, 0) << 10);
+  const float bound = bkey < 0x00800000u ? -INFINITY : key2f(bkey);
   return lower_preimage(bound, t_one, T, rT);
 }
 
@@ -1144,16 +1185,18 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
   if (u >= 1.0) u = 0x1.fffffffffffffp-1;
 
   const Feed fd1 = feed_first<E>(ctl, i, ln);
-  // one ring pass of this row, specialised on whether the penalty is on
-  auto first_pass = [&](auto&& body) {
-    if (R.pen) ring_pass<E, true>(sh, ln, fd1, nch, stage, R.rp, body);
-    else ring_pass<E, false>(sh, ln, fd1, nch, stage, R.rp, body);
+  RingWalk rw(sh, ln, fd1, stage);
+  // chunks [c0, c1) of this row's first pass, specialised on whether the penalty is on
+  auto first_range = [&](int c0, int c1, auto&& body) {
+    if (R.pen) ring_range<E, true>(sh, ln, fd1, rw, c0, c1, nch, R.rp, body);
+    else ring_range<E, false>(sh, ln, fd1, rw, c0, c1, nch, R.rp, body);
   };
 
   // ================================================================ first pass
   Stats S;
   float m0 = 0.0f;
-  uint32_t lumped = 0u;   // top-p: some e fell below the first locator level
+  bool over = false;      // GENERAL: some e >= 2^32 (the row maximum is far above m0)
+  uint32_t lumped = 0u;   // top-p: some e fell into the level's lumped last bucket
   float tau = -INFINITY;  // TOPK: bound on the k-th largest penalized logit
   // argmax bookkeeping for greedy rows: the largest value and the chunk it
   // was first seen in; the element index is recovered after the pass
@@ -1161,7 +1204,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
   int best_c = -1;
   if (mode == kGreedy) {
     float st = -INFINITY;
-    first_pass([&](int c, const float(&x)[EPT], int, bool) {
+    first_range(0, nch, [&](int c, const float(&x)[EPT], int, bool) {
       float mv = x[0];
 #pragma unroll
       for (int j = 1; j < EPT; ++j) mv = fmax_nan(mv, x[j]);
@@ -1173,12 +1216,14 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
     });
     S = block_stats(ctl, st, arg_of<E>(R, sh.bitmap, ln, best, best_c), 0.0, 0u, tid);
   } else if (mode == kTopk) {
-    float tmax = -INFINITY;
+    // the bound from chunk 0's thread maxima, refreshed after chunk kRefreshAt
+    float tmax = peek_max<E>(sh, ln, stage, R.pen, R.rp);
+    tau = topk_bound(R.k, R.t_one, R.T, R.rT, &ctl, sh.tm, tmax, tid);
     // each warp appends to its own list (slots counted in a warp-uniform register)
     unsigned long long* wl = sh.cand + warp * kWarpCands;
     int wcnt = 0;
     const uint32_t lt = (1u << lane) - 1u;
-    first_pass([&](int c, const float(&x)[EPT], int idx0, bool live) {
+    auto body = [&](int c, const float(&x)[EPT], int idx0, bool live) {
       float mv = x[0];
 #pragma unroll
       for (int j = 1; j < EPT; ++j) mv = fmax_nan(mv, x[j]);
@@ -1187,7 +1232,6 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
         best_c = c;
       }
       tmax = fmax_nan(tmax, mv);
-      if (c == 0 || c == kRefreshAt) tau = topk_bound(R.k, R.t_one, R.T, R.rT, &ctl, sh.tm, tmax, tid);
       if (__any_sync(0xffffffffu, live && mv >= tau)) {
 #pragma unroll
         for (int j = 0; j < EPT; ++j) {
@@ -1200,7 +1244,11 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
           wcnt += __popc(bal);
         }
       }
-    });
+    };
+    const int cr = min(kRefreshAt + 1, nch);
+    first_range(0, cr, body);
+    tau = topk_bound(R.k, R.t_one, R.T, R.rT, &ctl, sh.tm, tmax, tid);
+    first_range(cr, nch, body);
     if (lane == 0) ctl.red_j[warp] = wcnt;
     S = block_stats(ctl, tmax, R.greedy ? arg_of<E>(R, sh.bitmap, ln, best, best_c) : INT_MAX, 0.0, 0u, tid);
     if (!(S.nan || S.mx == INFINITY || S.mx == -INFINITY))
@@ -1209,9 +1257,18 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
     // GENERAL: e = exp(s - m0) with m0 the first chunk's maximum
     float lmax = -INFINITY;
     double lz = 0.0;
-    uint32_t over = 0u;
     const bool with_e = R.k == 0;  // large top-k computes its masses after the select
-    first_pass([&](int c, const float(&x)[EPT], int idx0, bool live) {
+    if (with_e) {
+      const float pm = peek_max<E>(sh, ln, stage, R.pen, R.rp);
+      const uint32_t wk = __reduce_max_sync(0xffffffffu, pm != pm ? 0u : f2key(pm));
+      if (lane == 0) ctl.red_b[warp] = wk;
+      __syncthreads();
+      uint32_t ck = 0u;
+      for (int w = 0; w < kWarps; ++w) ck = max(ck, ctl.red_b[w]);
+      const float mx = key2f(ck);
+      m0 = (mx > -INFINITY && mx < INFINITY) ? scaled(R, mx) : 0.0f;
+    }
+    first_range(0, nch, [&](int c, const float(&x)[EPT], int, bool) {
       float mv = x[0];
 #pragma unroll
       for (int j = 1; j < EPT; ++j) mv = fmax_nan(mv, x[j]);
@@ -1221,17 +1278,6 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       }
       lmax = fmax_nan(lmax, mv);
       if (!with_e) return;
-      if (c == 0) {
-        const bool nan = (lmax != lmax);
-        const uint32_t wk = __reduce_max_sync(0xffffffffu, nan ? 0u : f2key(lmax));
-        if (lane == 0) ctl.red_b[warp] = wk;
-        __syncthreads();
-        uint32_t ck = 0u;
-        for (int w = 0; w < kWarps; ++w) ck = max(ck, ctl.red_b[w]);
-        const float mx = key2f(ck);
-        m0 = (mx > -INFINITY && mx < INFINITY) ? scaled(R, mx) : 0.0f;
-      }
-      if (!live) return;
       float s[EPT];
       if (R.t_one) {
 #pragma unroll
@@ -1246,18 +1292,20 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
         const float e = exp_shifted(s[j], m0);
         part = __fadd_rn(part, e);
         if (want_hist) {
+          // no range test: e >= 2^32 and e < 2^-32 both clamp into the last bucket
           const uint32_t bits = __float_as_uint(e);
-          const uint32_t b = (kTopFine - bits) >> kShFine;
-          if (bits > kTopFine) over = 1u;  // e >= 2^32: the row maximum is far above m0
-          else if (b < (uint32_t)kBins) atomicAdd(&sh.hist[b], approx_mass13(bits));
-          else if (bits) lumped = 1u;      // 0 < e < 2^-32: below the level
+          atomicAdd(&sh.hist[min((kTopFine - bits) >> kShFine, (uint32_t)(kBins - 1))], approx_mass13(bits));
         }
       }
       lz += (double)part;
     });
-    S = block_stats(ctl, lmax, R.greedy ? arg_of<E>(R, sh.bitmap, ln, best, best_c) : INT_MAX, lz,
-                    over | (lumped << 1), tid);
+    S = block_stats(ctl, lmax, R.greedy ? arg_of<E>(R, sh.bitmap, ln, best, best_c) : INT_MAX, lz, 0u, tid);
+    if (with_e && !(S.nan || S.mx == INFINITY || S.mx == -INFINITY)) {
+      over = __float_as_uint(exp_shifted(scaled(R, S.mx), m0)) > kTopFine;
+      lumped = (want_hist && sh.hist[kBins - 1] != 0u) ? 1u : 0u;
+    }
   }
+  stage = (stage + nch) % kStages;
 
   if (a.out_penalized) {
     // debug output: the logits after the repetition penalty (sampler.py:31-38)
@@ -1442,7 +1490,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
   K.thr_idx = INT_MAX;
   double z = S.z;
   // the first pass's masses hold unless top-k comes first or e passed 2^32
-  const bool first_ok = R.k == 0 && !S.over;
+  const bool first_ok = R.k == 0 && !over;
   if (R.k > 0) {
     K.have_k = true;
     K.thr_k = scaled(R, radix_select<E>(R, sh, tid));
@@ -1455,7 +1503,6 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       for (int b = tid; b < kBins / 4; b += kThreads) reinterpret_cast<uint4*>(sh.hist)[b] = make_uint4(0, 0, 0, 0);
     __syncthreads();
     double lz = 0.0;
-    uint32_t lump = 0u;
     const bool hist = R.topp;
     global_pass<E>(R, sh.bitmap, tid, [&](int, const float(&x)[EPT], int, bool live) {
       if (!live) return;
@@ -1466,18 +1513,16 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
         part = __fadd_rn(part, e);
         if (hist) {
           const uint32_t bits = __float_as_uint(e);
-          const uint32_t b = (lv.top - bits) >> lv.sh;
-          if (bits <= lv.top && b < (uint32_t)kBins) atomicAdd(&sh.hist[b], approx_mass13(bits));
-          else if (bits) lump = 1u;
+          atomicAdd(&sh.hist[min((lv.top - bits) >> lv.sh, (uint32_t)(kBins - 1))], approx_mass13(bits));
         }
       }
       lz += (double)part;
     });
-    lumped = __syncthreads_or((int)lump) ? 1u : 0u;
+    __syncthreads();
+    lumped = (hist && sh.hist[kBins - 1] != 0u) ? 1u : 0u;
     if (!hist_only) z = block_segments(ctl, lz, tid);
   };
-  Level lv{kTopFine, kShFine};
-  lumped = S.lumped ? 1u : 0u;
+  Level lv{kTopFine, kShFine, true};
   if (!first_ok) {
     m0 = m;
     K.m0 = m0;
@@ -1490,7 +1535,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
     topp_window(&ctl, sh.hist, lv, 0.0, z, R.p, tid);
     if (!ctl.sel_found && lumped) {
       // the boundary may lie among masses below the level: locate it on the wide one
-      lv = Level{kTopWide, kShWide};
+      lv = Level{kTopWide, kShWide, true};
       stats_pass(lv, true);
       topp_window(&ctl, sh.hist, lv, 0.0, z, R.p, tid);
     }
@@ -1534,7 +1579,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
           la += (double)part;
         });
         const double above_lv = block_dsum(ctl, la, tid);
-        const Level lv2{win_hi, sh2};
+        const Level lv2{win_hi, sh2, false};
         topp_window(&ctl, sh.hist, lv2, above_lv, z, R.p, tid);
         if (ctl.sel_found) {
           lv = lv2;
@@ -1584,11 +1629,42 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
           }
         }
       };
-      if (ring2 && !ring_used) {
+      if (ring2 && !ring_used && !K.have_k) {
         ring_used = true;
         const Feed fd2 = feed_second<E>(ctl, i, ln, true);
-        if (R.pen) ring_pass<E, true>(sh, ln, fd2, nch, stage, R.rp, collect);
-        else ring_pass<E, false>(sh, ln, fd2, nch, stage, R.rp, collect);
+        const float mm = m0;
+        auto collect_ring = [&](int, const float(&x)[EPT], int idx0, bool) {
+          float s[EPT];
+          if (R.t_one) {
+#pragma unroll
+            for (int j = 0; j < EPT; ++j) s[j] = x[j];
+          } else {
+#pragma unroll
+            for (int j = 0; j < EPT; ++j) s[j] = div_by_const(x[j], R.T, R.rT);
+          }
+          float part = 0.0f;
+          bool anym = false;
+          uint32_t bits[EPT];
+#pragma unroll
+          for (int j = 0; j < EPT; ++j) {
+            const float e = exp_shifted(s[j], mm);
+            bits[j] = __float_as_uint(e);
+            part = bits[j] > whi ? __fadd_rn(part, e) : part;
+            anym |= (bits[j] - wlo) <= (whi - wlo);
+          }
+          la += (double)part;
+          if (anym) {
+#pragma unroll
+            for (int j = 0; j < EPT; ++j) {
+              if ((bits[j] - wlo) <= (whi - wlo)) {
+                const uint32_t slot = atomicAdd(&ctl.cand_n, 1u);
+                if (slot < (uint32_t)kCandCap) sh.cand[slot] = rank_key(s[j], idx0 + j);
+              }
+            }
+          }
+        };
+        if (R.pen) ring_pass<E, true>(sh, ln, fd2, nch, stage, R.rp, collect_ring);
+        else ring_pass<E, false>(sh, ln, fd2, nch, stage, R.rp, collect_ring);
       } else {
         global_pass<E>(R, sh.bitmap, tid, collect);
       }
