@@ -79,7 +79,7 @@ def measured_peaks():
 
 def profiled_traffic():
     """DRAM bytes per launch of the sampling kernel from the committed ncu summary."""
-    f = REPO / "profiles" / "sample_kernel_config2.md"
+    f = REPO / "profiles" / "row_kernel_config2.md"
     if not f.exists():
         return None
     m = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", f.read_text())

@@ -1404,8 +1404,13 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
     for (int i = tid; i < g.len; i += kThreads) {
       const float e = kept_mass(g, R, K, bitmap, i);
       if (a.out_probs) a.out_probs[out_off + i] = e > 0.f ? (float)((double)e / zkept) : 0.0f;
-      if (a.out_filtered)
-        a.out_filtered[out_off + i] = e > 0.f ? scaled(R, penalized_from_global(g, R, bitmap, i)) : -INFINITY;
+      if (a.out_filtered) {
+        // a zero mass is filtered out only behind a crossed top-p boundary
+        // (every positive mass ranks ahead of it); top-k alone keeps it
+        const float s = scaled(R, penalized_from_global(g, R, bitmap, i));
+        const bool keep = e > 0.f || (!K.window && (!K.have_thr_k || s >= K.thr_k_s));
+        a.out_filtered[out_off + i] = keep ? s : -INFINITY;
+      }
     }
   }
 }
