@@ -1117,6 +1117,184 @@ __device__ __forceinline__ int arg_of(const RowCtx& R, const uint32_t* bitmap, c
   return idx0 + jj;
 }
 
+// ---------------------------------------------------------------- top-p ties
+// Exact top-p decision for a window whose members overflow the candidate
+// list while the window is at single-value resolution (one bits(e) value per
+// bucket, at most kBins of them): each value's mass is count x e exactly, so
+// the crossing value e* and the number c of its members kept follow from
+// counts alone (sampler.py:66-70: rank j is kept iff j == 0 or cum[j-1] <=
+// top_p).  Members of e* rank by scaled logit, then index; a tie group's
+// kept members are its c of smallest index.  Members of e* with different
+// scaled logits (they lie within an ulp of e) set NS_STATUS_CAP_OVERFLOW and
+// are taken in index order.  Re-reads the row three times.  `above` is the
+// exact mass above the window, which ctl.seg holds per warp range; on return
+// ctl.seg includes the kept members, K describes the decision and the kept
+// total is returned.  Whole block.
+template <class E>
+__device__ __noinline__ double topp_ties(const RowCtx& R, const Sh& sh, Keep& K, uint32_t wlo, uint32_t whi,
+                                         double above, double z, uint32_t* status, int tid) {
+  constexpr int EPT = E::kEPT;
+  Ctl& ctl = *sh.ctl;
+  uint32_t* hist = sh.hist;
+  const int lane = tid & 31, warp = tid >> 5;
+  const uint32_t span_m1 = whi - wlo;  // < kBins
+  const Keep K1 = K;
+  // counts by value, bucket whi - bits(e)
+  for (int b = tid; b < kBins / 4; b += kThreads) reinterpret_cast<uint4*>(hist)[b] = make_uint4(0, 0, 0, 0);
+  if (tid == 0) {
+    ctl.misc = INT_MAX;
+    ctl.misc2 = -1;
+  }
+  __syncthreads();
+  global_pass<E>(R, sh.bitmap, tid, [&](int, const float(&x)[EPT], int, bool live) {
+    if (!live) return;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+      const uint32_t bits = __float_as_uint(K1.mass(scaled(R, x[j])));
+      if (bits - wlo <= span_m1) atomicAdd(&hist[whi - bits], 1u);
+    }
+  });
+  __syncthreads();
+  // the crossing value e*: thread t owns buckets [8t, 8t+8)
+  uint32_t cnt[8];
+  double m[8], tot = 0.0;
+  int last = -1;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int b = 8 * tid + j;
+    cnt[j] = (uint32_t)b <= span_m1 ? hist[b] : 0u;
+    m[j] = (double)cnt[j] * (double)__uint_as_float(whi - (uint32_t)b);
+    tot += m[j];
+    if (cnt[j]) last = b;
+  }
+  const double incl = warp_incl_f64(tot, lane);
+  if (lane == 31) ctl.red_e[warp] = incl;
+  if (last >= 0) atomicMax(&ctl.misc2, last);
+  __syncthreads();
+  double pre = above + incl - tot;
+  for (int w = 0; w < warp; ++w) pre += ctl.red_e[w];
+  {
+    double run = pre;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (cnt[j] && topp_crossed(run + m[j], z, R.p)) {
+        atomicMin(&ctl.misc, 8 * tid + j);
+        break;
+      }
+      run += m[j];
+    }
+  }
+  __syncthreads();
+  const bool none = ctl.misc == INT_MAX;  // no crossing inside: the whole window stays
+  const int bstar = none ? ctl.misc2 : ctl.misc;
+  const uint32_t estar = whi - (uint32_t)bstar;
+  const float ef = __uint_as_float(estar);
+  if (tid == (bstar >> 3)) {
+    // c: the fewest members of e* whose inclusive mass crosses
+    double p0 = pre;
+    for (int j = 0; j < (bstar & 7); ++j) p0 += m[j];
+    const uint32_t n = cnt[bstar & 7];
+    uint32_t lo = 1u, hi = n;
+    if (!none) {
+      while (lo < hi) {
+        const uint32_t mid = lo + (hi - lo) / 2u;
+        if (topp_crossed(p0 + (double)mid * (double)ef, z, R.p)) hi = mid;
+        else lo = mid + 1u;
+      }
+    }
+    ctl.sel_before = none ? n : lo;
+  }
+  __syncthreads();
+  const uint32_t c = ctl.sel_before;
+  // per warp range: members of e*, the range of their scaled logits, and the
+  // (kept) mass of the window above e*
+  uint32_t nme = 0u;
+  float smin = INFINITY, smax = -INFINITY;
+  double la = 0.0;
+  global_pass<E>(R, sh.bitmap, tid, [&](int, const float(&x)[EPT], int, bool live) {
+    if (!live) return;
+    float part = 0.0f;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+      const float s = scaled(R, x[j]);
+      const float e = K1.mass(s);
+      const uint32_t bits = __float_as_uint(e);
+      if (bits == estar) {
+        ++nme;
+        smin = fminf(smin, s);
+        smax = fmaxf(smax, s);
+      } else if (bits > estar && bits <= whi) {
+        part = __fadd_rn(part, e);
+      }
+    }
+    la += (double)part;
+  });
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    nme += __shfl_xor_sync(0xffffffffu, nme, o);
+    smin = fminf(smin, __shfl_xor_sync(0xffffffffu, smin, o));
+    smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, o));
+  }
+  const double wa = warp_dsum(la);
+  if (lane == 0) {
+    ctl.red_u[warp] = nme;
+    ctl.red_i[warp] = __float_as_int(smin);
+    ctl.red_j[warp] = __float_as_int(smax);
+  }
+  __syncthreads();
+  uint32_t pw = 0u;  // members of e* in the warp ranges before this one
+  for (int w = 0; w < warp; ++w) pw += ctl.red_u[w];
+  const uint32_t kc = c > pw ? min(nme, c - pw) : 0u;
+  if (lane == 0) ctl.seg[warp] += wa + (double)kc * (double)ef;
+  if (tid == 0) {
+    float a = INFINITY, b = -INFINITY;
+    for (int w = 0; w < kWarps; ++w) {
+      a = fminf(a, __int_as_float(ctl.red_i[w]));
+      b = fmaxf(b, __int_as_float(ctl.red_j[w]));
+    }
+    if (a != b && status) atomicOr(status, NS_STATUS_CAP_OVERFLOW);
+    ctl.dec_thr = -INFINITY;
+    ctl.dec_thr_idx = INT_MAX;
+  }
+  const double zk = above + block_dsum(ctl, la, tid) + (double)c * (double)ef;
+  // the warp holding the c-th member of e* finds it (index order)
+  const bool mine = nme > 0u && pw < c && c <= pw + nme;
+  const uint32_t target = c - pw;
+  uint32_t run = 0u;
+  bool done = !mine;
+  global_pass<E>(R, sh.bitmap, tid, [&](int, const float(&x)[EPT], int idx0, bool live) {
+    if (done) return;
+    uint32_t mask = 0u;
+    if (live) {
+#pragma unroll
+      for (int j = 0; j < EPT; ++j) mask |= (__float_as_uint(K1.mass(scaled(R, x[j]))) == estar ? 1u : 0u) << j;
+    }
+    const uint32_t n = (uint32_t)__popc(mask);
+    const uint32_t inc = warp_incl_u32(n, lane) + run;
+    const uint32_t hit = __ballot_sync(0xffffffffu, inc >= target && inc - n < target);
+    if (hit) {
+      if (lane == __ffs(hit) - 1) {
+        uint32_t k = target - (inc - n);
+        int j = 0;
+        for (; j < EPT; ++j)
+          if (((mask >> j) & 1u) && --k == 0u) break;
+        ctl.dec_thr = scaled(R, x[j]);
+        ctl.dec_thr_idx = idx0 + j;
+      }
+      done = true;
+    } else {
+      run = __shfl_sync(0xffffffffu, inc, 31);
+    }
+  });
+  __syncthreads();
+  K.window = true;
+  K.win_lo = wlo;
+  K.win_hi = whi;
+  K.thr = ctl.dec_thr;
+  K.thr_idx = ctl.dec_thr_idx;
+  return zk;
+}
+
 // ---------------------------------------------------------------- one row
 template <class E>
 __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, const Lane& ln, int& stage, int i,
@@ -1550,13 +1728,13 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
     int refines = 0;
     bool force_refine = false;
     while (crossed) {
-      if ((est > 0.9f * (float)kCandCap || force_refine) && lv.sh > 0 && refines < 3) {
+      if ((est > 0.9f * (float)kCandCap || force_refine) && lv.sh > 0 && refines < 5) {
         // ---- refine inside [win_lo, win_hi]: finer buckets, exact mass above the window
         const uint32_t span = win_hi - win_lo + 1u;
         int sh2 = 0;
         while (((span + (1u << sh2) - 1u) >> sh2) > (uint32_t)(kBins - 1)) ++sh2;
         if (sh2 >= lv.sh) {
-          refines = 3;  // the window is too wide to split further: collect it as it is
+          refines = 5;  // the window is too wide to split further: collect it as it is
           continue;
         }
         force_refine = false;
@@ -1587,7 +1765,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
           win_hi = lv.hi_key(ctl.sel_lo);
           est = ctl.sel_est;
         } else {
-          refines = 3;  // keep the previous window: it still contains the boundary
+          refines = 5;  // keep the previous window: it still contains the boundary
         }
         continue;
       }
@@ -1670,9 +1848,14 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       }
       const double above = block_segments(ctl, la, tid);
       const uint32_t ntot = ctl.cand_n;
-      if (ntot > (uint32_t)kCandCap && lv.sh > 0 && refines < 3) {
+      if (ntot > (uint32_t)kCandCap && lv.sh > 0 && refines < 5) {
         force_refine = true;  // the window held more elements than estimated
         continue;
+      }
+      if (ntot > (uint32_t)kCandCap && lv.sh == 0 && win_hi - max(win_lo, 1u) < (uint32_t)kBins) {
+        // a tie group (or many members of few values) at single-value resolution
+        zk = topp_ties<E>(R, sh, K, max(win_lo, 1u), win_hi, above, z, status, tid);
+        break;
       }
       // ---- decision on the sorted window members: the first rank whose
       // inclusive mass crosses (block-wide scan, 4 ranks per thread)

@@ -128,6 +128,13 @@ struct __align__(16) Ctl {
   unsigned long long wfix[kWarps];
   int32_t misc_i;
   int32_t misc_j;
+  // top-p tie resolution (leader broadcast, peer reports)
+  uint32_t bc_tie;
+  uint32_t bc_bits;
+  int32_t bc_q;
+  int32_t bc_cq;
+  float tie_smin[kCluster];
+  float tie_smax[kCluster];
   int32_t token;
   uint32_t mem_n;
 };
@@ -675,6 +682,312 @@ struct Shared {
   float* vals;
 };
 
+// ---------------------------------------------------------------- top-p ties
+// Exact top-p decision for a window whose members overflow the leader's list
+// while the window is at single-value resolution (one bits(e) value per
+// bucket, at most kBins of them).  Each value's mass is then count x e
+// exactly, so the crossing value e* and the number c of its members kept
+// follow from counts alone (sampler.py:66-70: rank j is kept iff j == 0 or
+// cum[j-1] <= top_p).  Members of one e* are ranked by scaled logit, then
+// index; when they share one scaled logit (a tie group) the kept ones are
+// the c of smallest index.  Members of e* with different scaled logits (they
+// would have to lie within an ulp of e) set NS_STATUS_CAP_OVERFLOW and are
+// taken in index order.  Whole cluster, three cluster barriers.  On return
+// K.thr / K.thr_idx name the last kept member, this CTA's dropped members
+// are zeroed in `vals`, its kept members' masses are added to ctl.wmass, and
+// owner / tloc / zkept describe the draw.
+__device__ __noinline__ void tie_resolve(const Geo& g, const Row& R, const Shared& sm, const Recv& rv, Keep& K,
+                                         uint32_t win_lo, uint32_t win_hi, double z, double u, uint32_t lead,
+                                         bool leader, int tid, uint32_t* status, int& owner, double& tloc,
+                                         double& zkept) {
+  Ctl& ctl = *sm.ctl;
+  uint32_t* hist = sm.hist;
+  float4* vals4 = reinterpret_cast<float4*>(sm.vals);
+  double* scr = reinterpret_cast<double*>(sm.keys);  // kCap doubles of scratch
+  const uint32_t* bitmap = sm.bitmap;
+  const int lane = tid & 31, warp = tid >> 5;
+  const uint32_t lo = max(win_lo, 1u);
+  const uint32_t span_m1 = win_hi - lo;  // < kBins
+
+  // A: this CTA's member counts by value, bucket win_hi - bits(e)
+  for (int i = tid; i < kBins / 4; i += kThreads) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
+  if (tid == 0) {
+    ctl.misc_i = INT_MAX;
+    ctl.misc_j = -1;
+  }
+  __syncthreads();
+  for (int f = g.f_begin + lane; f < g.f_end; f += 32) {
+    const float4 v = vals4[f];
+    const float t[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t bits = __float_as_uint(t[c]);
+      if (bits - lo <= span_m1) atomicAdd(&hist[win_hi - bits], 1u);
+    }
+  }
+  cluster_sync();  // every CTA's counts are complete
+
+  // B: the leader finds e*, c, the CTA q holding the c-th member of e* and
+  // the kept mass of every CTA, and broadcasts them
+  if (leader) {
+    double before = 0.0;
+    for (int r = 0; r < kCluster; ++r) before += rv.rec_above[r];
+    uint32_t cnt[8];
+    double m[8], tot = 0.0;
+    int last = -1;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int b = 8 * tid + j;
+      cnt[j] = 0u;
+      if ((uint32_t)b <= span_m1) {
+        const uint32_t ad = smem_addr(&hist[b]);
+#pragma unroll
+        for (int r = 0; r < kCluster; ++r) cnt[j] += dsmem_ld_u32(dsmem_map(ad, r));
+      }
+      m[j] = (double)cnt[j] * (double)__uint_as_float(win_hi - (uint32_t)b);
+      tot += m[j];
+      if (cnt[j]) last = b;
+    }
+    const double incl = warp_incl_f64(tot, lane);
+    if (lane == 31) scr[warp] = incl;
+    if (last >= 0) atomicMax(&ctl.misc_j, last);
+    __syncthreads();
+    double run = before + incl - tot;
+    for (int w = 0; w < warp; ++w) run += scr[w];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (cnt[j] && topp_crossed(run + m[j], z, R.p)) {
+        atomicMin(&ctl.misc_i, 8 * tid + j);
+        break;
+      }
+      run += m[j];
+    }
+    __syncthreads();
+    const bool none = ctl.misc_i == INT_MAX;  // no crossing in the window: keep all of it
+    const int bstar = none ? ctl.misc_j : ctl.misc_i;
+    const uint32_t estar_bits = win_hi - (uint32_t)max(bstar, 0);
+    // kept masses per CTA above e*, and the per-CTA counts of e*
+    double acc[kCluster];
+#pragma unroll
+    for (int r = 0; r < kCluster; ++r) acc[r] = 0.0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int b = 8 * tid + j;
+      if (b < bstar && cnt[j]) {
+        const uint32_t ad = smem_addr(&hist[b]);
+        const double e = (double)__uint_as_float(win_hi - (uint32_t)b);
+#pragma unroll
+        for (int r = 0; r < kCluster; ++r) acc[r] += (double)dsmem_ld_u32(dsmem_map(ad, r)) * e;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kCluster; ++r) {
+      const double s = warp_dsum(acc[r]);
+      if (lane == 0) scr[32 + warp * kCluster + r] = s;
+    }
+    if (bstar >= 0 && tid == (bstar >> 3)) {
+      // c: the smallest count of e* members whose inclusive mass crosses
+      double pre = before + incl - tot;  // the mass before e*
+      for (int w = 0; w < warp; ++w) pre += scr[w];
+      for (int j = 0; j < (bstar & 7); ++j) pre += m[j];
+      const uint32_t n = cnt[bstar & 7];
+      const double e = (double)__uint_as_float(estar_bits);
+      uint32_t c = n;
+      if (!none) {
+        uint32_t lo_c = 1u, hi_c = n;  // crossed(pre + hi_c * e) holds
+        while (lo_c < hi_c) {
+          const uint32_t mid = lo_c + (hi_c - lo_c) / 2u;
+          if (topp_crossed(pre + (double)mid * e, z, R.p)) hi_c = mid;
+          else lo_c = mid + 1u;
+        }
+        c = lo_c;
+      }
+      const uint32_t ad = smem_addr(&hist[bstar]);
+      uint32_t prefix = 0u;
+      int q = kCluster - 1;
+      uint32_t cq = 0u;
+      bool found = false;
+      for (int r = 0; r < kCluster; ++r) {
+        const uint32_t nr = dsmem_ld_u32(dsmem_map(ad, r));
+        const uint32_t cr = c > prefix ? min(nr, c - prefix) : 0u;
+        scr[32 + kWarps * kCluster + r] = (double)cr * e;
+        if (!found && nr > 0u && prefix + nr >= c) {
+          found = true;
+          q = r;
+          cq = c - prefix;
+        }
+        prefix += nr;
+      }
+      ctl.bc_q = q;
+      ctl.bc_cq = (int32_t)cq;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      double kept[kCluster], zk = 0.0;
+      for (int r = 0; r < kCluster; ++r) {
+        double s = rv.rec_above[r] + (bstar >= 0 ? scr[32 + kWarps * kCluster + r] : 0.0);
+        for (int w = 0; w < kWarps; ++w) s += scr[32 + w * kCluster + r];
+        kept[r] = s;
+        zk += s;
+      }
+      int own;
+      double t_own = 0.0;
+      pick_owner(kept, u * zk, own, t_own);
+      const int q = bstar >= 0 ? ctl.bc_q : -1;
+      const int cq = bstar >= 0 ? ctl.bc_cq : 0;
+      for (uint32_t r = 0; r < (uint32_t)kCluster; ++r) {
+        dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_bits), r), bstar >= 0 ? estar_bits : 0u);
+        dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_q), r), (uint32_t)q);
+        dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_cq), r), (uint32_t)cq);
+        dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_owner), r), (uint32_t)own);
+        dsmem_st_f64(dsmem_map(smem_addr(&ctl.bc_tloc), r), t_own);
+        dsmem_st_f64(dsmem_map(smem_addr(&ctl.bc_z), r), zk);
+      }
+    }
+  }
+  cluster_sync();  // decision delivered
+
+  // C: CTA q finds the cq-th member of e* in index order (the threshold
+  // element); every CTA reports the range of scaled logits among its e* members
+  const uint32_t estar = ctl.bc_bits;
+  const int q = ctl.bc_q;
+  {
+    float smin = INFINITY, smax = -INFINITY;
+    uint32_t ncount = 0u;
+    for (int f = g.f_begin + lane; f < g.f_end; f += 32) {
+      const float4 v = vals4[f];
+      const float t[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (__float_as_uint(t[c]) == estar && estar != 0u) {
+          const float s = scaled(R, penalized_from_global(g, R, bitmap, 4 * f + c));
+          smin = fminf(smin, s);
+          smax = fmaxf(smax, s);
+          ++ncount;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      smin = fminf(smin, __shfl_xor_sync(0xffffffffu, smin, o));
+      smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, o));
+      ncount += __shfl_xor_sync(0xffffffffu, ncount, o);
+    }
+    float* fs = reinterpret_cast<float*>(scr);
+    uint32_t* us = reinterpret_cast<uint32_t*>(scr) + 2 * kWarps;
+    if (lane == 0) {
+      fs[warp] = smin;
+      fs[kWarps + warp] = smax;
+      us[warp] = ncount;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float a = INFINITY, b = -INFINITY;
+      for (int w = 0; w < kWarps; ++w) {
+        a = fminf(a, fs[w]);
+        b = fmaxf(b, fs[kWarps + w]);
+      }
+      dsmem_st_f32(dsmem_map(smem_addr(&ctl.tie_smin[g.rank]), lead), a);
+      dsmem_st_f32(dsmem_map(smem_addr(&ctl.tie_smax[g.rank]), lead), b);
+    }
+    if ((int)g.rank == q) {
+      // the warp holding the cq-th member walks its piece
+      uint32_t target = (uint32_t)ctl.bc_cq;
+      int wsel = -1;
+      for (int w = 0; w < kWarps; ++w) {
+        if (us[w] >= target) { wsel = w; break; }
+        target -= us[w];
+      }
+      if (warp == wsel) {
+        uint32_t run = 0u;
+        for (int f0 = g.f_begin; f0 < g.f_end; f0 += 32) {
+          const int f = f0 + lane;
+          uint32_t mask = 0u;
+          if (f < g.f_end) {
+            const float4 v = vals4[f];
+            const float t[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) mask |= (__float_as_uint(t[c]) == estar ? 1u : 0u) << c;
+          }
+          const uint32_t n = (uint32_t)__popc(mask);
+          const uint32_t inc = warp_incl_u32(n, lane) + run;
+          const uint32_t hit = __ballot_sync(0xffffffffu, inc >= target && inc - n < target);
+          if (hit) {
+            if (lane == __ffs(hit) - 1) {
+              uint32_t k = target - (inc - n);  // 1-based within this lane's members
+              int c = 0;
+              for (; c < 4; ++c) {
+                if ((mask >> c) & 1u) {
+                  if (--k == 0u) break;
+                }
+              }
+              const int local = 4 * f + c;
+              const float s = scaled(R, penalized_from_global(g, R, bitmap, local));
+              for (uint32_t r = 0; r < (uint32_t)kCluster; ++r) {
+                dsmem_st_f32(dsmem_map(smem_addr(&ctl.bc_thr), r), s);
+                dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_thr_idx), r), (uint32_t)(g.base + local));
+              }
+            }
+            break;
+          }
+          run = __shfl_sync(0xffffffffu, inc, 31);
+        }
+      }
+    }
+    if (q < 0 && tid == 0) {
+      // nothing in the window: keep it all (the threshold is the last member)
+      ctl.bc_thr = -INFINITY;
+      ctl.bc_thr_idx = INT_MAX;
+    }
+  }
+  cluster_sync();  // threshold element and scaled-logit ranges delivered
+
+  if (leader && tid == 0 && q >= 0) {
+    float a = INFINITY, b = -INFINITY;
+    for (int r = 0; r < kCluster; ++r) {
+      a = fminf(a, ctl.tie_smin[r]);
+      b = fmaxf(b, ctl.tie_smax[r]);
+    }
+    if (a != b && status) atomicOr(status, NS_STATUS_CAP_OVERFLOW);
+  }
+  K.thr = ctl.bc_thr;
+  K.thr_idx = ctl.bc_thr_idx;
+  owner = ctl.bc_owner;
+  tloc = ctl.bc_tloc;
+  zkept = ctl.bc_z;
+
+  // D: drop this CTA's members ranked after the threshold element; add the
+  // kept ones to this warp's mass
+  double lane_kept = 0.0;
+  for (int f = g.f_begin + lane; f < g.f_end; f += 32) {
+    float4 v = vals4[f];
+    float t[4] = {v.x, v.y, v.z, v.w};
+    bool dirty = false;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t bits = __float_as_uint(t[c]);
+      if (bits - lo > span_m1) continue;
+      bool keep = bits > estar;
+      if (bits == estar) {
+        const int local = 4 * f + c;
+        const float s = scaled(R, penalized_from_global(g, R, bitmap, local));
+        keep = s > K.thr || (s == K.thr && g.base + local <= K.thr_idx);
+      }
+      if (keep) {
+        lane_kept += (double)t[c];
+      } else {
+        t[c] = 0.0f;
+        dirty = true;
+      }
+    }
+    if (dirty) vals4[f] = make_float4(t[0], t[1], t[2], t[3]);
+  }
+  const double wk = warp_dsum(lane_kept);
+  if (lane == 0) ctl.wmass[warp] += wk;
+  fence_proxy_async_smem();
+  __syncthreads();
+}
+
 // Samples `row` (its inputs are in ctl.rin[par]).  Every path issues this
 // warp's bulk copy of `next_row` as soon as the warp has finished with its
 // piece of the slice and records that in `prefetched`; the caller issues it
@@ -1214,7 +1527,7 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
       win_lo = lv.lo_key(ctl.sel_hi);
       win_hi = lv.hi_key(ctl.sel_lo);
       crossed = true;
-      if (ctl.sel_est <= 0.9f * (float)kCap || lv.sh == 0 || lvl >= 2) break;
+      if (ctl.sel_est <= 0.9f * (float)kCap || lv.sh == 0 || lvl >= 5) break;
       // refine inside [win_lo, win_hi]: finer buckets, exact mass above the window
       const uint32_t span = win_hi - win_lo + 1u;
       int sh2 = 0;
@@ -1334,46 +1647,53 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
           int own;
           double t_own = 0.0;
           pick_owner(kept, u * zk, own, t_own);
+          // too many members, but one bits(e) value per bucket: exact by counts
+          const bool tie = ntot > (uint32_t)kCap && lv.sh == 0 && (win_hi - win_lo) < (uint32_t)kBins;
           if (lane < kCluster) {
             const uint32_t r = (uint32_t)lane;
+            dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_tie), r), tie ? 1u : 0u);
             dsmem_st_f32(dsmem_map(smem_addr(&ctl.bc_thr), r), thr);
             dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_thr_idx), r), (uint32_t)thr_idx);
             dsmem_st_u32(dsmem_map(smem_addr(&ctl.bc_owner), r), (uint32_t)own);
             dsmem_st_f64(dsmem_map(smem_addr(&ctl.bc_tloc), r), t_own);
             dsmem_st_f64(dsmem_map(smem_addr(&ctl.bc_z), r), zk);
           }
-          if (ntot > (uint32_t)kCap && lane == 0 && status) atomicOr(status, NS_STATUS_CAP_OVERFLOW);
+          if (ntot > (uint32_t)kCap && !tie && lane == 0 && status) atomicOr(status, NS_STATUS_CAP_OVERFLOW);
         }
       }
       cluster_sync();  // barrier: decision delivered
       K.window = true;
       K.win_lo = win_lo;
       K.win_hi = win_hi;
-      K.thr = ctl.bc_thr;
-      K.thr_idx = ctl.bc_thr_idx;
-      owner = ctl.bc_owner;
-      tloc = ctl.bc_tloc;
-      zkept = ctl.bc_z;
       keep_lo = win_lo;
-      // drop this CTA's members ranked after the threshold element and add
-      // the kept ones to the per-warp masses (fixed point: order-independent)
-      if (tid < kWarps) ctl.wfix[tid] = 0ull;
-      __syncthreads();
-      const int nm = (int)min(ctl.mem_n, (uint32_t)kCap);
-      for (int i = tid; i < nm; i += kThreads) {
-        const float sm_s = sm.mem_s[i];
-        const int li = sm.mem_i[i];
-        if (sm_s < K.thr || (sm_s == K.thr && g.base + li > K.thr_idx)) {
-          vals[li] = 0.0f;
-        } else {
-          const int w = min(kWarps - 1, (li >> 2) / g.chunk);
-          atomicAdd(&ctl.wfix[w], (unsigned long long)llrint((double)sm.mem_e[i] * kFixedScale));
+      if (ctl.bc_tie) {
+        tie_resolve(g, R, sm, rv, K, win_lo, win_hi, z, u, lead, leader, tid, status, owner, tloc, zkept);
+      } else {
+        K.thr = ctl.bc_thr;
+        K.thr_idx = ctl.bc_thr_idx;
+        owner = ctl.bc_owner;
+        tloc = ctl.bc_tloc;
+        zkept = ctl.bc_z;
+        // drop this CTA's members ranked after the threshold element and add
+        // the kept ones to the per-warp masses (fixed point: order-independent)
+        if (tid < kWarps) ctl.wfix[tid] = 0ull;
+        __syncthreads();
+        const int nm = (int)min(ctl.mem_n, (uint32_t)kCap);
+        for (int i = tid; i < nm; i += kThreads) {
+          const float sm_s = sm.mem_s[i];
+          const int li = sm.mem_i[i];
+          if (sm_s < K.thr || (sm_s == K.thr && g.base + li > K.thr_idx)) {
+            vals[li] = 0.0f;
+          } else {
+            const int w = min(kWarps - 1, (li >> 2) / g.chunk);
+            atomicAdd(&ctl.wfix[w], (unsigned long long)llrint((double)sm.mem_e[i] * kFixedScale));
+          }
         }
+        fence_proxy_async_smem();  // the zeroed elements may sit in another warp's piece
+        __syncthreads();
+        if (tid < kWarps) ctl.wmass[tid] += (double)ctl.wfix[tid] * kFixedToReal;
+        __syncthreads();
       }
-      fence_proxy_async_smem();  // the zeroed elements may sit in another warp's piece
-      __syncthreads();
-      if (tid < kWarps) ctl.wmass[tid] += (double)ctl.wfix[tid] * kFixedToReal;
-      __syncthreads();
     }
   }
   if (!topp || !crossed) {

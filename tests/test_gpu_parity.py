@@ -202,3 +202,34 @@ def test_fallback_paths():
     u = np.random.default_rng(5).random(len(rows)).astype(np.float32)
     gpu = H.run_cabi(lg, params, hists, u)
     _check(H.compare(gpu, np.stack(rows), params, hists, u))
+
+
+@pytest.mark.parametrize("V", [32768, 128256])
+def test_tie_groups_at_the_top_p_boundary(V):
+    """Tie groups larger than any candidate list straddle the top-p boundary:
+    exactly the first ranks (value descending, index ascending) are kept."""
+    dev = _dev()
+    rng = np.random.default_rng(33)
+    SP = importlib.import_module(H.PKG + ".config").SamplingParams
+    rows, params, hists = [], [], []
+
+    def add(x, p, h=()):
+        rows.append(np.asarray(x, dtype=np.float32))
+        params.append(p)
+        hists.append(list(h))
+
+    base = lambda: (rng.standard_normal(V) * 2.0).astype(np.float32)  # noqa: E731
+    add(np.full(V, 1.5), SP(temperature=1.0, top_p=0.9))                       # one group: the whole row
+    add(np.full(V, -3.25), SP(temperature=0.7, top_p=0.37))                    # same, tempered
+    x = np.full(V, 1.0); x[rng.permutation(V)[: V // 2]] = 2.0
+    add(x, SP(temperature=1.0, top_p=0.5))                                     # boundary inside the top group
+    add(x, SP(temperature=1.0, top_p=0.95))                                    # boundary inside the lower group
+    add(np.round(base()), SP(temperature=1.0, top_p=0.6))                      # integer logits: big groups
+    add(np.round(base()), SP(temperature=0.8, top_p=0.8, repetition_penalty=1.2),
+        rng.integers(0, V, 300).tolist())                                      # with penalty
+    add(np.full(V, 0.5), SP(temperature=1.0, top_k=5000, top_p=0.5))          # top-k ties, then top-p
+    lg = torch.from_numpy(np.stack(rows)).to(dev)
+    u = np.random.default_rng(6).random(len(rows)).astype(np.float32)
+    gpu = H.run_cabi(lg, params, hists, u)
+    assert gpu["status"] == 0
+    _check(H.compare(gpu, np.stack(rows), params, hists, u))
