@@ -62,8 +62,11 @@ extern "C" {
 #define NS_STATUS_BAD_SAMPLE_INDEX 0x1u /* sample_indices[i] out of range */
 #define NS_STATUS_BAD_HISTORY_ID 0x2u   /* history id outside [0, vocab)  */
 #define NS_STATUS_WAIT_TIMEOUT 0x4u     /* a bounded wait gave up         */
-#define NS_STATUS_CAP_OVERFLOW 0x8u     /* candidate list overflowed; the
-                                           row fell back to keeping ties  */
+#define NS_STATUS_CAP_OVERFLOW 0x8u     /* a top-p boundary fell among more
+                                           members than the kernel ranks
+                                           exactly (distinct logits within
+                                           one fp32 mass value); the row
+                                           kept them in index order       */
 
 /* One row's sampling parameters (32 bytes, device array [num_rows]).
  * Mirrors nanoserve/config.py:68-79 SamplingParams (temperature :72,

@@ -1651,8 +1651,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
         return;
       }
     }
-    // a warp's candidate list overflowed: the row takes the general path
-    if (tid == 0 && status) atomicOr(status, NS_STATUS_CAP_OVERFLOW);
+    // a warp's candidate list overflowed: the row takes the (exact) general path
     mode = kGeneral;
   }
 

@@ -1383,8 +1383,7 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
       }
       return;
     }
-    // the candidate list overflowed: this row takes the general path
-    if (leader && tid == 0 && status) atomicOr(status, NS_STATUS_CAP_OVERFLOW);
+    // the candidate list overflowed: this row takes the (exact) general path
     need_min = true;
   }
 

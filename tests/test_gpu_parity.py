@@ -201,6 +201,7 @@ def test_fallback_paths():
     lg = torch.from_numpy(np.stack(rows)).to(dev)
     u = np.random.default_rng(5).random(len(rows)).astype(np.float32)
     gpu = H.run_cabi(lg, params, hists, u)
+    assert gpu["status"] == 0  # every fallback here is exact
     _check(H.compare(gpu, np.stack(rows), params, hists, u))
 
 
