@@ -228,8 +228,8 @@ def run_ours(args):
         cpu = cpu_baseline_single()
 
     params, hist = make_host_workload(rank)
-    pk = packing.pack(params, hist, VOCAB)
-    rp, off, ids = sampler_mod.upload_packed(pk, dev)
+    pk = packing.pack(params, hist, VOCAB, sms=torch.cuda.get_device_properties(dev).multi_processor_count)
+    rp, off, ids, order = sampler_mod.upload_packed(pk, dev)
     logits = make_device_logits(torch, dev, COPIES, 1234 + rank)
     hist_bytes = int(pk.ids.nbytes)
     algo_bytes = ROWS * VOCAB * 4 + hist_bytes
@@ -240,7 +240,8 @@ def run_ours(args):
     seed = 2024
 
     def step(k: int, with_comm: bool = True):
-        s.sample_packed(logits[k % COPIES], rp, off, ids, out=out, seed=seed, offset=k, row_offset=rank * ROWS)
+        s.sample_packed(logits[k % COPIES], rp, off, ids, out=out, seed=seed, offset=k, row_offset=rank * ROWS,
+                        row_order=order)
         if world > 1 and with_comm:
             dist.all_gather_into_tensor(gathered, out)
 
@@ -367,7 +368,7 @@ def run_ours(args):
         dist.all_reduce(t_e, op=dist.ReduceOp.MAX)
     e2e_ms = float(t_e.item())
     del toks
-    packed_bytes = packing.layout(pk)[3]
+    packed_bytes = packing.layout(pk)[-1]
 
     graphs.clear()
     if world > 1:

@@ -10,8 +10,10 @@
  * sampler.py:31-38, temperature sampler.py:40-51, top-k sampler.py:53-58,
  * top-p sampler.py:60-73, softmax + NaN guard sampler.py:75-80, greedy
  * argmax sampler.py:82-83, multinomial sampler.py:84-89).  Here the whole
- * chain is one kernel launch per call: one HBM pass per vocabulary row,
- * the row held in the shared memory of an 8-CTA thread-block cluster.
+ * chain is one kernel launch per call with one HBM pass per vocabulary row:
+ * batches of 32 or more aligned rows take one thread block per row that
+ * streams the row through shared memory; smaller batches take an 8-CTA
+ * thread-block cluster per row that holds it in distributed shared memory.
  *
  * Everything in this header is plain C: raw pointers, sizes and a stream
  * handle.  All pointers named "device" must be CUDA device (or managed)
@@ -36,7 +38,7 @@
 extern "C" {
 #endif
 
-#define NS_ABI_VERSION 1
+#define NS_ABI_VERSION 2
 
 /* status codes returned by every entry point */
 #define NS_OK 0
@@ -67,6 +69,8 @@ extern "C" {
                                            exactly (distinct logits within
                                            one fp32 mass value); the row
                                            kept them in index order       */
+#define NS_STATUS_BAD_ROW_ORDER 0x10u   /* row_order[t] outside [0, S): that
+                                           slot took row t instead        */
 
 /* One row's sampling parameters (32 bytes, device array [num_rows]).
  * Mirrors nanoserve/config.py:68-79 SamplingParams (temperature :72,
@@ -123,6 +127,14 @@ typedef struct NsSampleArgs {
   float* out_probs;                  /* device [S, V] or NULL              */
   uint32_t* status;                  /* device [1] or NULL: NS_STATUS_* bits
                                         OR-ed in by the kernel             */
+  const int32_t* row_order;          /* device [S] or NULL: the order in
+                                        which the kernel takes rows, a
+                                        permutation of [0, S).  A scheduling
+                                        hint only: outputs do not depend on
+                                        it.  Putting the most expensive rows
+                                        (top-p without top-k) where they
+                                        share no SM with each other shortens
+                                        mixed batches. */
 } NsSampleArgs;
 
 /* Enqueue one sampling step on `stream` (a cudaStream_t; NULL = legacy

@@ -33,6 +33,7 @@ NS_STATUS_BAD_SAMPLE_INDEX = 0x1
 NS_STATUS_BAD_HISTORY_ID = 0x2
 NS_STATUS_WAIT_TIMEOUT = 0x4
 NS_STATUS_CAP_OVERFLOW = 0x8
+NS_STATUS_BAD_ROW_ORDER = 0x10
 
 # every entry point the header declares
 EXPORTED_SYMBOLS = ("ns_sample", "ns_last_error", "ns_abi_version", "ns_max_vocab")
@@ -72,6 +73,7 @@ class NsSampleArgs(ctypes.Structure):
         ("out_filtered", ctypes.c_void_p),
         ("out_probs", ctypes.c_void_p),
         ("status", ctypes.c_void_p),
+        ("row_order", ctypes.c_void_p),
     ]
 
 

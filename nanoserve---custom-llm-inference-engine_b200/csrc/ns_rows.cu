@@ -163,7 +163,7 @@ struct __align__(16) RowIn {
   NsRowParams P;
   int64_t h[2];
   int64_t src;
-  int64_t pad;
+  int64_t row;  // the row this slot samples (row_order applied)
 };
 
 // Where a row comes from and how often the ring streams it.
@@ -245,6 +245,7 @@ struct Lane {
   int tid, lane, warp;
   int base;  // element index of this thread's first element in chunk 0
   int nv;    // chunks in which this thread holds elements
+  int nvw;   // chunks in which every lane of this warp holds elements
 };
 
 template <class E>
@@ -256,6 +257,7 @@ __device__ __forceinline__ Lane make_lane(int V, int W, int tid) {
   ln.base = ln.warp * W + ln.lane * E::kEPT;
   const int ww = max(0, min(W, V - ln.warp * W));  // this warp's range length
   ln.nv = ww > ln.lane * E::kEPT ? (ww - ln.lane * E::kEPT + E::kPiece - 1) / E::kPiece : 0;
+  ln.nvw = ww > 31 * E::kEPT ? (ww - 31 * E::kEPT + E::kPiece - 1) / E::kPiece : 0;
   return ln;
 }
 
@@ -372,12 +374,14 @@ struct RingWalk {
   uint32_t slot, ring_lo, ring_hi;
   const char* gp;
   int left;
+  int plain_end;  // chunks below this refill from `cur` in every lane of the warp
   __device__ __forceinline__ RingWalk(const Sh& sh, const Lane& ln, const Feed& fd, int stage) {
     ring_lo = smem_addr(sh.ring) + ln.tid * 16;
     ring_hi = ring_lo + kStages * kChunkBytes;
     slot = ring_lo + stage * kChunkBytes;
     gp = fd.cur + kStages * kPieceBytes;
     left = fd.cur ? ln.nv - kStages : 0;
+    plain_end = fd.cur ? ln.nvw - kStages : 0;
   }
   // refill the slot just read with chunk c + kStages (one commit group); a
   // slot this lane has no data for is filled with -inf logits instead
@@ -403,8 +407,40 @@ template <class E, bool PEN, class F>
 __device__ __forceinline__ void ring_range(const Sh& sh, const Lane& ln, const Feed& fd, RingWalk& rw, int c0, int c1,
                                            int nch, float rp, F&& body) {
   constexpr int EPT = E::kEPT;
+  int c = c0;
   int idx0 = ln.base + c0 * E::kPiece;
-  for (int c = c0; c < c1; ++c, idx0 += E::kPiece) {
+  // whole turns of the ring in which every lane of the warp has data and
+  // refills from the current source: fixed slot addresses, immediate source
+  // offsets, no per-chunk bookkeeping (the bound is warp-uniform, so bodies
+  // may use warp collectives)
+  const int cm = min(c1, rw.plain_end);
+  if (c + kStages <= cm) {
+    uint32_t slots[kStages];
+#pragma unroll
+    for (int u = 0; u < kStages; ++u) {
+      const uint32_t a = rw.slot + u * kChunkBytes;
+      slots[u] = a >= rw.ring_hi ? a - kStages * kChunkBytes : a;
+    }
+    const char* gp = rw.gp;
+    do {
+#pragma unroll
+      for (int u = 0; u < kStages; ++u) {
+        cp_async_wait_ring();
+        const typename E::Raw raw = E::lds_s(slots[u]);
+        cp_async16_s(slots[u], gp + u * kPieceBytes);
+        cp_async_commit();
+        float x[EPT];
+        penalized<E, PEN>(sh.bitmap, rp, raw, idx0 + u * E::kPiece, x);
+        body(c + u, x, idx0 + u * E::kPiece, true);
+      }
+      c += kStages;
+      idx0 += kStages * E::kPiece;
+      gp += kStages * kPieceBytes;
+    } while (c + kStages <= cm);
+    rw.left -= c - c0;
+    rw.gp = gp;
+  }
+  for (; c < c1; ++c, idx0 += E::kPiece) {
     cp_async_wait_ring();
     const typename E::Raw raw = E::lds_s(rw.slot);
     rw.refill(fd, ln, c, nch, E::kNegInf2);
@@ -483,13 +519,19 @@ __device__ __forceinline__ void global_pass(const RowCtx& R, const uint32_t* bit
 
 // Threads 0..3 copy row `row`'s inputs (64 bytes) into `dst` with plain
 // loads; cp.async is kept for the ring, whose group count must stay exact.
-__device__ __forceinline__ void fetch_row_inputs(const NsSampleArgs& a, RowIn& dst, int row, int tid) {
+__device__ __forceinline__ void fetch_row_inputs(const NsSampleArgs& a, RowIn& dst, int ticket, int tid) {
   if (tid >= 4) return;
+  int row = ticket;
+  if (a.row_order) {
+    const int r = __ldg(&a.row_order[ticket]);
+    if (r >= 0 && r < a.num_rows) row = r;
+    else if (tid == 3 && a.status) atomicOr(a.status, NS_STATUS_BAD_ROW_ORDER);
+  }
   uint4 v;
   if (tid < 2) {
     v = __ldg(reinterpret_cast<const uint4*>(&a.row_params[row]) + tid);
   } else {
-    int64_t x0, x1 = 0;
+    int64_t x0, x1 = row;
     if (tid == 2) {
       x0 = a.history_offsets ? a.history_offsets[row] : 0;
       x1 = a.history_offsets ? a.history_offsets[row + 1] : 0;
@@ -501,10 +543,11 @@ __device__ __forceinline__ void fetch_row_inputs(const NsSampleArgs& a, RowIn& d
   reinterpret_cast<uint4*>(&dst)[tid] = v;
 }
 
-// Plan of this block's i-th row (global row `row`), from its fetched inputs.
-__device__ __forceinline__ void make_plan(const NsSampleArgs& a, Ctl& ctl, int i, int row, bool debug) {
+// Plan of this block's i-th row (taken at position `ticket` of the row
+// order), from its fetched inputs.
+__device__ __forceinline__ void make_plan(const NsSampleArgs& a, Ctl& ctl, int i, int ticket, bool debug) {
   RowPlan& pl = ctl.plan[i & 1];
-  if (row >= a.num_rows) {
+  if (ticket >= a.num_rows) {
     pl.valid = 0;
     return;
   }
@@ -1969,22 +2012,22 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const NsSampleArgs a, 
   Ctl& ctl = *sh.ctl;
   const int tid = threadIdx.x;
   const int G = gridDim.x;
-  const int row0 = blockIdx.x;
+  const int t0 = blockIdx.x;  // this block takes positions t0, t0 + G, ... of the row order
   const bool debug = (a.out_filtered != nullptr) || (a.out_probs != nullptr);
   const Lane ln = make_lane<E>(a.vocab_size, W, tid);
 
-  if (row0 < a.num_rows) fetch_row_inputs(a, ctl.rin[0], row0, tid);
-  if (row0 + G < a.num_rows) fetch_row_inputs(a, ctl.rin[1], row0 + G, tid);
+  if (t0 < a.num_rows) fetch_row_inputs(a, ctl.rin[0], t0, tid);
+  if (t0 + G < a.num_rows) fetch_row_inputs(a, ctl.rin[1], t0 + G, tid);
   __syncthreads();
-  if (tid == 0) make_plan(a, ctl, 0, row0, debug);
+  if (tid == 0) make_plan(a, ctl, 0, t0, debug);
   __syncthreads();
   ring_start<E>(ctl, sh.ring, ln);
   int stage = 0;
-  for (int i = 0, row = row0; row < a.num_rows; ++i, row += G) {
+  for (int i = 0, t = t0; t < a.num_rows; ++i, t += G) {
     __syncthreads();  // the previous row is finished; row i+1's inputs are in place
-    if (tid == 0) make_plan(a, ctl, i + 1, row + G, debug);
-    if (row + 2 * G < a.num_rows) fetch_row_inputs(a, ctl.rin[(i + 2) & 3], row + 2 * G, tid);
-    sample_row<E>(a, sh, ln, stage, i, row, nch, W);
+    if (tid == 0) make_plan(a, ctl, i + 1, t + G, debug);
+    if (t + 2 * G < a.num_rows) fetch_row_inputs(a, ctl.rin[(i + 2) & 3], t + 2 * G, tid);
+    sample_row<E>(a, sh, ln, stage, i, (int)ctl.rin[i & 3].row, nch, W);
   }
   cp_async_wait_all();  // nothing may land in shared memory after the block exits
 }

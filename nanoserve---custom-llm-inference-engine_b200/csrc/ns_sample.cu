@@ -342,6 +342,17 @@ __device__ __forceinline__ void fetch_row_inputs(const NsSampleArgs& a, RowIn& d
   if (tid < 4) cp_async_commit();
 }
 
+// Row taken at position t of the row order (NsSampleArgs.row_order, a
+// scheduling hint); an entry outside [0, S) takes row t and, with `flag`,
+// sets NS_STATUS_BAD_ROW_ORDER.
+__device__ __forceinline__ int ordered_row(const NsSampleArgs& a, int t, bool flag) {
+  if (!a.row_order) return t;
+  const int r = __ldg(&a.row_order[t]);
+  if (r >= 0 && r < a.num_rows) return r;
+  if (flag && a.status) atomicOr(a.status, NS_STATUS_BAD_ROW_ORDER);
+  return t;
+}
+
 // Smallest float c <= b with RN(c/T) == RN(b/T): the lower end of the set of
 // logits whose scaled value is at least RN(b/T).
 __device__ float lower_preimage(const Row& R, float b) {
@@ -1786,15 +1797,16 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
     for (int i = tid; i < (int)(2 * sizeof(Recv) / 16); i += kThreads) r4[i] = make_uint4(0, 0, 0, 0);
   }
   if (cid < nrows) {
-    fetch_row_inputs(a, ctl.rin[0], cid, tid);
+    fetch_row_inputs(a, ctl.rin[0], ordered_row(a, cid, false), tid);
     if (tid < 4) cp_async_wait_all();
   }
   __syncthreads();
   cluster_sync();  // every CTA of the cluster runs and is initialised
-  if (cid < nrows) issue_chunk(S, g, ctl, sm.vals, cid, warp, lane);
+  if (cid < nrows) issue_chunk(S, g, ctl, sm.vals, ordered_row(a, cid, false), warp, lane);
 
   uint32_t it = 0;
-  for (int row = cid; row < nrows; row += ncl, ++it) {
+  for (int t = cid; t < nrows; t += ncl, ++it) {
+    const int row = ordered_row(a, t, tid == 0 && g.rank == 0);
     __syncthreads();  // the previous row is finished in this CTA
     // clear what peers will write for the next row (they write it only after
     // this row's first cluster barrier, which waits for this CTA)
@@ -1802,7 +1814,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const NsSampleArgs 
       uint4* r4 = reinterpret_cast<uint4*>(&sm.recv[(it & 1u) ^ 1u]);
       for (int i = tid; i < (int)(sizeof(Recv) / 16); i += kThreads) r4[i] = make_uint4(0, 0, 0, 0);
     }
-    const int next = (row + ncl < nrows) ? row + ncl : -1;
+    const int next = (t + ncl < nrows) ? ordered_row(a, t + ncl, false) : -1;
     if (next >= 0) fetch_row_inputs(a, ctl.rin[(it & 1u) ^ 1u], next, tid);
     bool prefetched = false;
     process_row(a, S, g, sm, row, next, it & 1u, it & (kCluster - 1), tid, prefetched);

@@ -30,13 +30,14 @@ void check_opt(const c10::optional<at::Tensor>& t, const at::Device& dev, const 
 
 // sample(logits, sample_indices, row_params, history_offsets, history_ids,
 //        uniforms, philox_seed, philox_offset, row_offset, out,
-//        out_penalized, out_filtered, out_probs, status) -> ()
+//        out_penalized, out_filtered, out_probs, status, row_order) -> ()
 void sample_op(const at::Tensor& logits, const c10::optional<at::Tensor>& sample_indices,
                const at::Tensor& row_params, const c10::optional<at::Tensor>& history_offsets,
                const c10::optional<at::Tensor>& history_ids, const c10::optional<at::Tensor>& uniforms,
                int64_t philox_seed, int64_t philox_offset, int64_t row_offset, at::Tensor& out,
                const c10::optional<at::Tensor>& out_penalized, const c10::optional<at::Tensor>& out_filtered,
-               const c10::optional<at::Tensor>& out_probs, const c10::optional<at::Tensor>& status) {
+               const c10::optional<at::Tensor>& out_probs, const c10::optional<at::Tensor>& status,
+               const c10::optional<at::Tensor>& row_order) {
   TORCH_CHECK(logits.dim() == 2, "logits must be 2-D [rows, vocab]");
   TORCH_CHECK(logits.is_cuda(), "logits must be a CUDA tensor");
   TORCH_CHECK(logits.stride(1) == 1, "logits rows must be contiguous");
@@ -59,6 +60,9 @@ void sample_op(const at::Tensor& logits, const c10::optional<at::Tensor>& sample
   check_opt(out_filtered, dev, "out_filtered", at::kFloat);
   check_opt(out_probs, dev, "out_probs", at::kFloat);
   check_opt(status, dev, "status", at::kInt);
+  check_opt(row_order, dev, "row_order", at::kInt);
+  if (row_order.has_value() && row_order->defined())
+    TORCH_CHECK(row_order->numel() == S, "row_order must have one element per row");
   if (sample_indices.has_value() && sample_indices->defined())
     TORCH_CHECK(sample_indices->numel() == S, "sample_indices must have one element per row");
   if (uniforms.has_value() && uniforms->defined())
@@ -92,6 +96,7 @@ void sample_op(const at::Tensor& logits, const c10::optional<at::Tensor>& sample
   a.out_filtered = static_cast<float*>(const_cast<void*>(opt_ptr(out_filtered)));
   a.out_probs = static_cast<float*>(const_cast<void*>(opt_ptr(out_probs)));
   a.status = static_cast<uint32_t*>(const_cast<void*>(opt_ptr(status)));
+  a.row_order = static_cast<const int32_t*>(opt_ptr(row_order));
   const int rc = ns_sample(&a, c10::cuda::getCurrentCUDAStream(dev.index()).stream());
   TORCH_CHECK(rc == NS_OK, "ns_sample failed (", rc, "): ", ns_last_error());
 }
@@ -103,7 +108,7 @@ TORCH_LIBRARY(nanoserve_b200, m) {
       "sample(Tensor logits, Tensor? sample_indices, Tensor row_params, Tensor? history_offsets, "
       "Tensor? history_ids, Tensor? uniforms, int philox_seed, int philox_offset, int row_offset, "
       "Tensor(a!) out, Tensor(b!)? out_penalized, Tensor(c!)? out_filtered, Tensor(d!)? out_probs, "
-      "Tensor(e!)? status) -> ()");
+      "Tensor(e!)? status, Tensor? row_order=None) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(nanoserve_b200, CUDA, m) { m.impl("sample", &sample_op); }

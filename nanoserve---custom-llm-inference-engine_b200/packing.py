@@ -13,6 +13,9 @@ which filters run are made here exactly as the reference makes them:
   (sampler.py:33).  Only those rows' histories are shipped, and their ids
   must lie in ``[0, vocab)``; otherwise ``IndexError`` is raised, as the
   reference's ``index_select`` does (sampler.py:35).
+
+It also builds the optional row order (``NsSampleArgs.row_order``), a
+scheduling hint that spreads the expensive rows over the GPU's SMs.
 """
 from __future__ import annotations
 
@@ -61,6 +64,57 @@ def derive_row(p, vocab: int, hist_len: int) -> tuple:
     return (np.float32(temp), top_p32, np.float32(rp), k_eff, flags, 0, seed_u64)
 
 
+# Relative cost of a row on the one-block-per-row kernel, by the path it
+# takes there (greedy; top-k <= 128 with or without top-p; top-p alone, large
+# top-k or plain sampling), from measured single-row times on B200.
+TOPK_LIST_MAX = 128
+COST_GREEDY, COST_TOPK, COST_PLAIN, COST_TOPP, COST_LARGE_K = 1, 3, 5, 7, 8
+ROWS_PER_SM = 2  # resident blocks per SM of the one-block-per-row kernel
+
+
+def row_costs(row_params: np.ndarray) -> np.ndarray:
+    """Cost class of every packed row (larger = longer on its SM)."""
+    flags = row_params["flags"]
+    k = row_params["top_k"]
+    greedy = (flags & _cabi.NS_ROW_GREEDY) != 0
+    topp = (flags & _cabi.NS_ROW_TOP_P) != 0
+    cost = np.full(row_params.shape[0], COST_PLAIN, dtype=np.int32)
+    cost[topp] = COST_TOPP
+    cost[k > TOPK_LIST_MAX] = COST_LARGE_K
+    cost[(k > 0) & (k <= TOPK_LIST_MAX)] = COST_TOPK
+    cost[greedy] = COST_GREEDY
+    return cost
+
+
+def schedule(row_params: np.ndarray, sms: int, per_sm: int = ROWS_PER_SM) -> np.ndarray:
+    """Row order for ``NsSampleArgs.row_order``.
+
+    The kernel's block b takes positions b, b + G, b + 2G, ... of the order
+    (G = min(S, per_sm * sms) blocks), and blocks b and b + sms share an SM.
+    Each round of G positions gives the first slot of every SM one of the
+    most expensive rows left and the SM's second slot one of the cheapest
+    left, so that no SM holds two expensive rows while another idles.
+    """
+    S = row_params.shape[0]
+    order = np.arange(S, dtype=np.int32)
+    if S == 0 or sms <= 0:
+        return order
+    by_cost = np.argsort(-row_costs(row_params), kind="stable").astype(np.int32)
+    G = min(S, per_sm * sms)
+    lo, hi, t = 0, S, 0
+    while t < S:
+        n = min(G, S - t)
+        n1 = min(n, sms)
+        n2 = n - n1
+        order[t : t + n1] = by_cost[lo : lo + n1]
+        lo += n1
+        if n2:
+            order[t + n1 : t + n] = by_cost[hi - n2 : hi][::-1]
+            hi -= n2
+        t += n
+    return order
+
+
 @dataclass
 class Packed:
     """Packed host arrays, all little-endian numpy."""
@@ -68,13 +122,15 @@ class Packed:
     row_params: np.ndarray  # ROW_DTYPE [S]
     offsets: np.ndarray     # int64 [S+1]
     ids: np.ndarray         # int32 [N]
+    order: Optional[np.ndarray] = None  # int32 [S] row order, or None
 
     @property
     def num_rows(self) -> int:
         return int(self.row_params.shape[0])
 
 
-def pack(params: Sequence, histories: Sequence[Sequence[int]], vocab: int) -> Packed:
+def pack(params: Sequence, histories: Sequence[Sequence[int]], vocab: int, sms: Optional[int] = None) -> Packed:
+    """Pack one step's rows; with ``sms`` (the GPU's SM count) also their row order."""
     S = len(params)
     if len(histories) < S:
         raise IndexError("history_token_ids has fewer entries than sampling_params_list")
@@ -100,24 +156,28 @@ def pack(params: Sequence, histories: Sequence[Sequence[int]], vocab: int) -> Pa
         ids = ids64.astype(np.int32)
     else:
         ids = np.zeros(0, dtype=np.int32)
-    return Packed(rows, offsets, ids)
+    order = schedule(rows, sms) if sms else None
+    return Packed(rows, offsets, ids, order)
 
 
-def layout(packed: Packed) -> tuple[int, int, int, int]:
-    """Byte offsets of (row_params, offsets, ids) in one staging buffer, and its size."""
+def layout(packed: Packed) -> tuple[int, int, int, int, int]:
+    """Byte offsets of (row_params, offsets, ids, order) in one staging buffer, and its size."""
     a = 0
     b = (a + packed.row_params.nbytes + 15) & ~15
     c = (b + packed.offsets.nbytes + 15) & ~15
-    end = (c + packed.ids.nbytes + 15) & ~15
-    return a, b, c, max(end, 16)
+    d = (c + packed.ids.nbytes + 15) & ~15
+    end = (d + (packed.order.nbytes if packed.order is not None else 0) + 15) & ~15
+    return a, b, c, d, max(end, 16)
 
 
 def to_bytes(packed: Packed, out: Optional[np.ndarray] = None) -> np.ndarray:
-    """Serialise into one uint8 buffer (row_params | offsets | ids)."""
-    a, b, c, end = layout(packed)
+    """Serialise into one uint8 buffer (row_params | offsets | ids | order)."""
+    a, b, c, d, end = layout(packed)
     if out is None:
         out = np.zeros(end, dtype=np.uint8)
     out[a : a + packed.row_params.nbytes] = packed.row_params.view(np.uint8)
     out[b : b + packed.offsets.nbytes] = packed.offsets.view(np.uint8)
     out[c : c + packed.ids.nbytes] = packed.ids.view(np.uint8)
+    if packed.order is not None:
+        out[d : d + packed.order.nbytes] = packed.order.view(np.uint8)
     return out

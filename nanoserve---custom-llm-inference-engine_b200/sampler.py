@@ -98,12 +98,12 @@ class Sampler:
         S = len(sampling_params_list)
         if sample_indices is None and logits.shape[0] != S:
             raise ValueError(f"logits has {logits.shape[0]} rows but {S} sampling params were given")
-        packed = packing.pack(sampling_params_list, history_token_ids, vocab)
-        row_params, offsets, ids = self._upload(packed, logits.device)
+        packed = packing.pack(sampling_params_list, history_token_ids, vocab, sms=_sm_count(logits.device))
+        row_params, offsets, ids, order = self._upload(packed, logits.device)
         return self.sample_packed(
             logits, row_params, offsets, ids,
             sample_indices=sample_indices, uniforms=uniforms, seed=seed,
-            out_dtype=out_dtype, return_debug=return_debug,
+            out_dtype=out_dtype, return_debug=return_debug, row_order=order,
         )
 
     # -- pre-packed device inputs (graph-capturable) ------------------------
@@ -122,7 +122,12 @@ class Sampler:
         out: Optional[torch.Tensor] = None,
         out_dtype: torch.dtype = torch.int64,
         return_debug: bool = False,
+        row_order: Optional[torch.Tensor] = None,
     ):
+        """One step over pre-packed device inputs (``packing.pack`` + ``upload_packed``).
+
+        ``row_order`` (int32 [S], a permutation) only changes the order in
+        which the kernel takes rows, never the result."""
         S = row_params.numel() // packing.ROW_DTYPE.itemsize
         dev = logits.device
         if logits.stride(1) != 1:
@@ -147,14 +152,14 @@ class Sampler:
             logits, sample_indices, row_params, history_offsets, history_ids, uniforms,
             int(seed) & 0x7FFFFFFFFFFFFFFF, int(offset), int(row_offset), out,
             dbg["penalized"] if dbg else None, dbg["filtered"] if dbg else None,
-            dbg["probs"] if dbg else None, dbg["status"] if dbg else None,
+            dbg["probs"] if dbg else None, dbg["status"] if dbg else None, row_order,
         )
         if return_debug:
             return out, dbg
         return out
 
     def _upload(self, packed: packing.Packed, device: torch.device):
-        a, b, c, end = packing.layout(packed)
+        a, b, c, d, end = packing.layout(packed)
         host = self._staging.get(end)
         packing.to_bytes(packed, host.numpy())
         dev = host.to(device, non_blocking=True)
@@ -166,11 +171,13 @@ class Sampler:
         ids = dev[c : c + packed.ids.nbytes].view(torch.int32) if packed.ids.size else None
         if ids is None:
             offsets = None
-        return row_params, offsets, ids
+        order = dev[d : d + packed.order.nbytes].view(torch.int32) if packed.order is not None else None
+        return row_params, offsets, ids, order
 
 
 def upload_packed(packed: packing.Packed, device) -> tuple:
-    """Device tensors (row_params uint8, offsets int64 or None, ids int32 or None)."""
+    """Device tensors (row_params uint8, offsets int64 or None, ids int32 or
+    None, row order int32 or None) for :meth:`Sampler.sample_packed`."""
     device = torch.device(device)
     rp = torch.from_numpy(packed.row_params.view(np.uint8).copy()).to(device)
     if packed.ids.size:
@@ -178,4 +185,17 @@ def upload_packed(packed: packing.Packed, device) -> tuple:
         ids = torch.from_numpy(packed.ids.copy()).to(device)
     else:
         off, ids = None, None
-    return rp, off, ids
+    order = torch.from_numpy(packed.order.copy()).to(device) if packed.order is not None else None
+    return rp, off, ids, order
+
+
+_SMS: dict = {}
+
+
+def _sm_count(device) -> int:
+    """SM count of a CUDA device (cached)."""
+    device = torch.device(device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SMS:
+        _SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SMS[idx]

@@ -234,3 +234,33 @@ def test_tie_groups_at_the_top_p_boundary(V):
     gpu = H.run_cabi(lg, params, hists, u)
     assert gpu["status"] == 0
     _check(H.compare(gpu, np.stack(rows), params, hists, u))
+
+
+def test_row_order_changes_nothing_but_the_schedule():
+    """NsSampleArgs.row_order is a scheduling hint: any permutation gives the
+    same tokens and debug outputs; an out-of-range entry is flagged and that
+    slot takes its own row."""
+    dev = _dev()
+    w = W.make(2, rows=256)
+    lg = torch.from_numpy(w.logits).to(dev)
+    u, si = w.uniforms, w.sample_indices
+    perm = np.random.default_rng(3).permutation(256).astype(np.int32)
+    sched = H.packing.pack(w.params, w.histories, lg.shape[1], sms=148).order
+    for debug in (False, True):
+        base = H.run_cabi(lg, w.params, w.histories, u, sample_indices=si, debug=debug)
+        for order in (perm, sched):
+            got = H.run_cabi(lg, w.params, w.histories, u, sample_indices=si, debug=debug,
+                             row_order=torch.from_numpy(order).to(dev))
+            assert got["status"] == base["status"] == 0
+            assert np.array_equal(got["tokens"], base["tokens"])
+            for key in ("penalized", "filtered", "probs"):
+                if key in base:
+                    assert np.array_equal(got[key].view(np.uint32), base[key].view(np.uint32)), key
+    bad = np.arange(256, dtype=np.int32)
+    bad[5] = -1
+    bad[9] = 256
+    base = H.run_cabi(lg, w.params, w.histories, u, sample_indices=si, debug=False)
+    got = H.run_cabi(lg, w.params, w.histories, u, sample_indices=si, debug=False,
+                     row_order=torch.from_numpy(bad).to(dev))
+    assert got["status"] == H.cabi.NS_STATUS_BAD_ROW_ORDER
+    assert np.array_equal(got["tokens"], base["tokens"])

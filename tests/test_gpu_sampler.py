@@ -87,7 +87,7 @@ def test_sampler_graph_capture():
     lg = torch.from_numpy(w.logits).to(dev)
     s = NS.Sampler(dev)
     pk = H.packing.pack(w.params, w.histories, lg.shape[1])
-    rp, off, ids = importlib.import_module(H.PKG + ".sampler").upload_packed(pk, dev)
+    rp, off, ids, _ = importlib.import_module(H.PKG + ".sampler").upload_packed(pk, dev)
     out = torch.empty(16, dtype=torch.int64, device=dev)
     uni = torch.from_numpy(w.uniforms).to(dev)
     s.sample_packed(lg, rp, off, ids, uniforms=uni, out=out, offset=0)

@@ -69,7 +69,7 @@ def test_csr_only_ships_penalised_rows():
     assert pk.ids.tolist() == [1, 2, 2, 7]
     assert pk.ids.dtype == np.int32
     buf = packing.to_bytes(pk)
-    a, b, c, end = packing.layout(pk)
+    a, b, c, d, end = packing.layout(pk)
     assert buf.size == end and end % 16 == 0
     assert np.array_equal(buf[c:c + 16].view(np.int32), pk.ids)
 
@@ -90,3 +90,32 @@ def test_row_params_byte_layout():
     assert raw[0:4].view(np.float32)[0] == np.float32(0.5)
     assert raw[12:16].view(np.int32)[0] == 7
     assert raw[24:32].view(np.uint64)[0] == 9
+
+
+def test_schedule_is_a_permutation_that_spreads_expensive_rows():
+    W = importlib.import_module(PKG_NAME + ".workloads")
+    sms = 148
+    for S in (1, 7, 148, 256, 296, 1000):
+        pk = packing.pack(W.mixed_params(S), [[]] * S, V, sms=sms)
+        order = pk.order
+        assert order.dtype == np.int32 and sorted(order.tolist()) == list(range(S))
+    # config 2: blocks b and b + sms share an SM; no SM gets two top-p rows,
+    # and every top-p row shares its SM with the cheapest rows there are
+    pk = packing.pack(W.mixed_params(256), [[]] * 256, V, sms=sms)
+    cost = packing.row_costs(pk.row_params)[pk.order]
+    pair = cost[:sms].copy()
+    pair[: 256 - sms] += cost[sms:]
+    assert pair.max() <= packing.COST_TOPP + packing.COST_GREEDY
+    assert (cost[:64] == packing.COST_TOPP).all()
+    # without an SM count there is no order; layout then has an empty order region
+    pk = packing.pack(W.mixed_params(8), [[]] * 8, V)
+    a, b, c, d, end = packing.layout(pk)
+    assert pk.order is None and end >= d
+
+
+def test_order_travels_in_the_staging_buffer():
+    W = importlib.import_module(PKG_NAME + ".workloads")
+    pk = packing.pack(W.mixed_params(300), [[]] * 300, V, sms=148)
+    buf = packing.to_bytes(pk)
+    a, b, c, d, end = packing.layout(pk)
+    assert d % 16 == 0 and np.array_equal(buf[d : d + 4 * 300].view(np.int32), pk.order)
