@@ -174,19 +174,23 @@ __device__ __forceinline__ float exp_shifted(float s, float m) {
 // that guard the result equals x / t bit for bit for every fp32 x; this was
 // checked exhaustively over all 2^32 inputs for ten divisors from 1e-6 to
 // 1e30 (tests/test_division_identity.py re-checks a sample on the CPU).
+// The IEEE division, out of line: streaming loops that may need it (rarely)
+// keep only a call, so their hot code stays small.
+static __device__ __noinline__ float div_rn_out_of_line(float x, float t) { return __fdiv_rn(x, t); }
+
 __device__ __forceinline__ float div_by_const(float x, float t, float r) {
   float q0 = __fmul_rn(x, r);
   float rem = __fmaf_rn(-q0, t, x);
   float q = __fmaf_rn(rem, r, q0);
   float ax = fabsf(x), aq = fabsf(q0);
-  if (!(fminf(ax, aq) >= 0x1p-60f && fmaxf(ax, aq) <= 0x1p+100f)) q = __fdiv_rn(x, t);
+  if (!(fminf(ax, aq) >= 0x1p-60f && fmaxf(ax, aq) <= 0x1p+100f)) q = div_rn_out_of_line(x, t);
   return q;
 }
 
 // Repetition penalty on one logit (HF rule, nanoserve/scheduler/sampler.py:37):
 // negative scores are multiplied by rp, others divided by rp (IEEE fp32).
 __device__ __forceinline__ float penalize(float x, float rp) {
-  return (x < 0.0f) ? __fmul_rn(x, rp) : __fdiv_rn(x, rp);
+  return (x < 0.0f) ? __fmul_rn(x, rp) : div_rn_out_of_line(x, rp);
 }
 
 // Approximate mass of one positive normal float for the top-p locator

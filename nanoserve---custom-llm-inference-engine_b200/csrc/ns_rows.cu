@@ -1338,6 +1338,34 @@ __device__ __noinline__ double topp_ties(const RowCtx& R, const Sh& sh, Keep& K,
   return zk;
 }
 
+// ---------------------------------------------------------------- top-k lists
+// One chunk's logits of a thread, passed by value to out-of-line helpers.
+template <class E>
+struct Chunk {
+  float v[E::kEPT];
+};
+
+// Appends this warp's elements >= tau of one chunk to the warp's candidate
+// list (slots counted in the warp-uniform wcnt; entries past kWarpCands are
+// counted but not stored) and returns the new count.  Rare once the bound is
+// tight, so it stays out of the streaming loop.  Whole warp.
+template <class E>
+__device__ __noinline__ int topk_insert(unsigned long long* wl, int wcnt, const Chunk<E> ch, int idx0, float tau,
+                                        bool live, bool t_one, float T, float rT, int lane) {
+  const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll
+  for (int j = 0; j < E::kEPT; ++j) {
+    const bool tk = live && (ch.v[j] >= tau);
+    const uint32_t bal = __ballot_sync(0xffffffffu, tk);
+    if (tk) {
+      const int slot = wcnt + __popc(bal & lt);
+      if (slot < kWarpCands) wl[slot] = rank_key(t_one ? ch.v[j] : div_by_const(ch.v[j], T, rT), idx0 + j);
+    }
+    wcnt += __popc(bal);
+  }
+  return wcnt;
+}
+
 // ---------------------------------------------------------------- one row
 template <class E>
 __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, const Lane& ln, int& stage, int i,
@@ -1443,7 +1471,6 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
     // each warp appends to its own list (slots counted in a warp-uniform register)
     unsigned long long* wl = sh.cand + warp * kWarpCands;
     int wcnt = 0;
-    const uint32_t lt = (1u << lane) - 1u;
     auto body = [&](int c, const float(&x)[EPT], int idx0, bool live) {
       float mv = x[0];
 #pragma unroll
@@ -1454,16 +1481,10 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       }
       tmax = fmax_nan(tmax, mv);
       if (__any_sync(0xffffffffu, live && mv >= tau)) {
+        Chunk<E> ch;
 #pragma unroll
-        for (int j = 0; j < EPT; ++j) {
-          const bool tk = live && (x[j] >= tau);
-          const uint32_t bal = __ballot_sync(0xffffffffu, tk);
-          if (tk) {
-            const int slot = wcnt + __popc(bal & lt);
-            if (slot < kWarpCands) wl[slot] = rank_key(scaled(R, x[j]), idx0 + j);
-          }
-          wcnt += __popc(bal);
-        }
+        for (int j = 0; j < EPT; ++j) ch.v[j] = x[j];
+        wcnt = topk_insert<E>(wl, wcnt, ch, idx0, tau, live, R.t_one, R.T, R.rT, lane);
       }
     };
     const int cr = min(kRefreshAt + 1, nch);

@@ -89,11 +89,11 @@ def row_costs(row_params: np.ndarray) -> np.ndarray:
 def schedule(row_params: np.ndarray, sms: int, per_sm: int = ROWS_PER_SM) -> np.ndarray:
     """Row order for ``NsSampleArgs.row_order``.
 
-    The kernel's block b takes positions b, b + G, b + 2G, ... of the order
-    (G = min(S, per_sm * sms) blocks), and blocks b and b + sms share an SM.
-    Each round of G positions gives the first slot of every SM one of the
-    most expensive rows left and the SM's second slot one of the cheapest
-    left, so that no SM holds two expensive rows while another idles.
+    The row kernel's block b takes positions b, b + G, b + 2G, ... of the
+    order (G = min(S, per_sm * sms) blocks, per_sm of them on each SM).
+    Each round of G positions gives the first sms blocks, which the hardware
+    spreads one per SM, the most expensive rows left, and the other blocks
+    the cheapest left, so that expensive rows do not pile up on few SMs.
     """
     S = row_params.shape[0]
     order = np.arange(S, dtype=np.int32)
