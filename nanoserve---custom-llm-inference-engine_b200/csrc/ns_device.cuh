@@ -192,6 +192,11 @@ __device__ __forceinline__ float div_by_const(float x, float t, float r) {
 __device__ __forceinline__ float penalize(float x, float rp) {
   return (x < 0.0f) ? __fmul_rn(x, rp) : div_rn_out_of_line(x, rp);
 }
+// The same with rrp = RN(1/rp): the division by the row constant rp goes
+// through div_by_const (bit-exact, IEEE division only at extreme operands).
+__device__ __forceinline__ float penalize(float x, float rp, float rrp) {
+  return (x < 0.0f) ? __fmul_rn(x, rp) : div_by_const(x, rp, rrp);
+}
 
 // Approximate mass of one positive normal float for the top-p locator
 // histogram: the top 16 of its 24 significand bits.  Every element of one
@@ -247,6 +252,15 @@ __device__ __forceinline__ double warp_incl_f64(double v, int lane) {
 // inclusive mass passes this test is the last one kept.
 __device__ __forceinline__ bool topp_crossed(double cum, double z, float p) {
   return (float)(cum / z) > p;
+}
+
+// The same test without a division: fp32(cum / z) > p exactly when cum / z
+// lies above the midpoint between p and the next float up, so with
+// thr = topp_threshold(z, p) the test is cum > thr (the two differ only
+// where cum / z is within a double rounding of that midpoint).
+__device__ __forceinline__ double topp_threshold(double z, float p) {
+  const float up = __uint_as_float(__float_as_uint(p) + (p >= 0.0f ? 1u : -1u));
+  return 0.5 * ((double)p + (double)up) * z;
 }
 
 // Sort key: ascending keys give (value descending, index ascending).

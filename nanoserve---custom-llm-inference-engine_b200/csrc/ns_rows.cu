@@ -63,8 +63,6 @@ constexpr int kStages = 6;                // ring depth (chunks in flight per th
 constexpr int kPieceBytes = 512;          // one warp's share of a chunk
 constexpr int kChunkBytes = kWarps * kPieceBytes;
 constexpr int kBins = 4096;               // top-p locator histogram (u32 approximate masses)
-constexpr int kCoarse = 64;               // coarse buckets of kFine fine buckets
-constexpr int kFine = kBins / kCoarse;
 constexpr int kTmBins = 2048;             // per-thread-maximum histogram, quarter binades
 constexpr int kTmShift = 21;
 constexpr int kRadixBins = 2048;          // radix-select level histogram (u32 counts)
@@ -80,6 +78,8 @@ constexpr double kSlack = 1.0 + 0x1p-11;  // > 1 / (1 - 2^-12): locator mass err
 constexpr int kMinVocab = 24576;          // a row spans more chunks than the ring has stages
 constexpr int kMaxVocab = 196608;
 constexpr int kMaxChunks = (kMaxVocab / kWarps + 127) / 128;  // pieces per warp range (fp32)
+constexpr int kPiecesMax = (kMaxChunks + kStages - 1) / kStages;  // draw pieces (kStages chunks) per warp range
+constexpr int kSub = 256;                  // top-p member sub-buckets
 
 // ---------------------------------------------------------------- element formats
 // 16 bytes of a row as logits.
@@ -178,6 +178,8 @@ struct __align__(16) Ctl {
   RowPlan plan[2];
   double seg[kWarps];        // kept mass per warp range
   double piece[kMaxChunks];  // kept mass per piece of the drawn warp range
+  double pm[kWarps][kPiecesMax];  // top-p: kept mass per kStages-chunk piece of every warp range
+  unsigned long long dec_key;     // top-p: rank key of the last kept member
   uint32_t red_k[kWarps];
   uint32_t red_b[kWarps];
   int32_t red_i[kWarps];
@@ -185,7 +187,6 @@ struct __align__(16) Ctl {
   uint32_t red_u[kWarps];
   uint32_t red_o[kWarps];
   double red_e[kWarps];
-  double cmass[kCoarse];
   double pick_t;
   double dec_z;
   float sel_est;
@@ -232,10 +233,16 @@ struct Sh {
 };
 
 // One row being sampled, with the row layout shared by every row.
+// Repetition penalty of a row: rp and RN(1/rp).
+struct Pen {
+  float rp, rrp;
+};
+
 struct RowCtx {
   const char* src;
   int V, W, nch, row;
   float T, rT, rp, p;
+  Pen pp;
   int k;  // top-k (0: none)
   bool t_one, greedy, topp, pen;
 };
@@ -289,7 +296,7 @@ __device__ __noinline__ float lower_preimage(float b, bool t_one, float T, float
 
 // The thread's 16 bytes of a row as penalized logits (sampler.py:31-38).
 template <class E, bool PEN>
-__device__ __forceinline__ void penalized(const uint32_t* bitmap, float rp, const typename E::Raw& raw, int idx0,
+__device__ __forceinline__ void penalized(const uint32_t* bitmap, Pen pp, const typename E::Raw& raw, int idx0,
                                           float (&x)[E::kEPT], bool live = true) {
   E::unpack(raw, x);
   if (PEN && live) {
@@ -297,7 +304,7 @@ __device__ __forceinline__ void penalized(const uint32_t* bitmap, float rp, cons
     if (m) {
 #pragma unroll
       for (int j = 0; j < E::kEPT; ++j)
-        if ((m >> j) & 1u) x[j] = penalize(x[j], rp);
+        if ((m >> j) & 1u) x[j] = penalize(x[j], pp.rp, pp.rrp);
     }
   }
 }
@@ -405,7 +412,7 @@ struct RingWalk {
 // no element: live false).
 template <class E, bool PEN, class F>
 __device__ __forceinline__ void ring_range(const Sh& sh, const Lane& ln, const Feed& fd, RingWalk& rw, int c0, int c1,
-                                           int nch, float rp, F&& body) {
+                                           int nch, Pen pp, F&& body) {
   constexpr int EPT = E::kEPT;
   int c = c0;
   int idx0 = ln.base + c0 * E::kPiece;
@@ -430,7 +437,7 @@ __device__ __forceinline__ void ring_range(const Sh& sh, const Lane& ln, const F
         cp_async16_s(slots[u], gp + u * kPieceBytes);
         cp_async_commit();
         float x[EPT];
-        penalized<E, PEN>(sh.bitmap, rp, raw, idx0 + u * E::kPiece, x);
+        penalized<E, PEN>(sh.bitmap, pp, raw, idx0 + u * E::kPiece, x);
         body(c + u, x, idx0 + u * E::kPiece, true);
       }
       c += kStages;
@@ -446,27 +453,27 @@ __device__ __forceinline__ void ring_range(const Sh& sh, const Lane& ln, const F
     rw.refill(fd, ln, c, nch, E::kNegInf2);
     const bool live = c < ln.nv;
     float x[EPT];
-    penalized<E, PEN>(sh.bitmap, rp, raw, idx0, x, live);
+    penalized<E, PEN>(sh.bitmap, pp, raw, idx0, x, live);
     body(c, x, idx0, live);
   }
 }
 template <class E, bool PEN, class F>
-__device__ __forceinline__ void ring_pass(const Sh& sh, const Lane& ln, const Feed& fd, int nch, int& stage, float rp,
+__device__ __forceinline__ void ring_pass(const Sh& sh, const Lane& ln, const Feed& fd, int nch, int& stage, Pen pp,
                                           F&& body) {
   RingWalk rw(sh, ln, fd, stage);
-  ring_range<E, PEN>(sh, ln, fd, rw, 0, nch, nch, rp, body);
+  ring_range<E, PEN>(sh, ln, fd, rw, 0, nch, nch, pp, body);
   stage = (stage + nch) % kStages;
 }
 
 // Maximum of this thread's penalized logits in the pass's first chunk, read
 // ahead of the pass (which then finds the chunk already landed).
 template <class E>
-__device__ __forceinline__ float peek_max(const Sh& sh, const Lane& ln, int stage, bool pen, float rp) {
+__device__ __forceinline__ float peek_max(const Sh& sh, const Lane& ln, int stage, bool pen, Pen pp) {
   cp_async_wait_ring();
   const typename E::Raw raw = E::lds_s(smem_addr(sh.ring) + stage * kChunkBytes + ln.tid * 16);
   float x[E::kEPT];
-  if (pen) penalized<E, true>(sh.bitmap, rp, raw, ln.base, x, ln.nv > 0);
-  else penalized<E, false>(sh.bitmap, rp, raw, ln.base, x);
+  if (pen) penalized<E, true>(sh.bitmap, pp, raw, ln.base, x, ln.nv > 0);
+  else penalized<E, false>(sh.bitmap, pp, raw, ln.base, x);
   float mv = x[0];
 #pragma unroll
   for (int j = 1; j < E::kEPT; ++j) mv = fmax_nan(mv, x[j]);
@@ -505,8 +512,8 @@ __device__ __forceinline__ void global_pass(const RowCtx& R, const uint32_t* bit
         const bool live = c < ln.nv;
         float x[EPT];
         if (live) {
-          if (R.pen) penalized<E, true>(bitmap, R.rp, raw[u], idx0, x);
-          else penalized<E, false>(bitmap, R.rp, raw[u], idx0, x);
+          if (R.pen) penalized<E, true>(bitmap, R.pp, raw[u], idx0, x);
+          else penalized<E, false>(bitmap, R.pp, raw[u], idx0, x);
         } else {
 #pragma unroll
           for (int j = 0; j < EPT; ++j) x[j] = -INFINITY;
@@ -887,87 +894,72 @@ __device__ __noinline__ float radix_select(const RowCtx R, const Sh sh, int tid)
 
 // ---------------------------------------------------------------- top-p window
 // Reference rule (sampler.py:66-70): sorted rank j is kept iff j == 0 or
-// float32(cum[j-1]) <= top_p; topp_crossed() is the test on inclusive mass.
-// Finds the bucket window [lo, hi] of level `lv` that must contain the first
-// crossing, given that each bucket's approximate mass is within a factor
-// (1 - 2^-12) of its exact mass, plus an estimate of its element count.
-// `base` is the exact mass above the level's range, `z` the row total.
-__device__ __noinline__ void topp_window(Ctl* ctlp, const uint32_t* h, const Level lv, double base, double z,
-                                         float p, int tid) {
+// float32(cum[j-1]) <= top_p; with thr = topp_threshold(z, top_p) the rank
+// whose inclusive mass first exceeds thr is the last one kept.  Finds the
+// bucket window [lo, hi] of level `lv` that must contain that rank, given
+// that each bucket's approximate mass is within a factor (1 - 2^-12) of its
+// exact mass: lo is the first bucket whose inclusive mass times kSlack passes
+// thr, hi the first whose inclusive mass does (the level's last bucket when
+// none does).  `base` is the exact mass above the level's range.  Also sets
+// an estimate of the number of elements in the window.  Whole block: thread
+// t owns buckets [8t, 8t + 8) and one block scan orders them.
+__device__ __noinline__ void topp_window(Ctl* ctlp, const uint32_t* h, const Level lv, double base, double thr,
+                                         int tid) {
+  constexpr int kPer = kBins / kThreads;
+  static_assert(kPer == 8, "two 16-byte loads per thread");
   Ctl& ctl = *ctlp;
   const int lane = tid & 31, warp = tid >> 5;
-  {
-    // coarse sums: 8 threads per coarse bucket, 8 fine buckets each
-    const int c = tid >> 3;
-    double m = 0.0;
+  const uint4 q0 = reinterpret_cast<const uint4*>(h)[2 * tid];
+  const uint4 q1 = reinterpret_cast<const uint4*>(h)[2 * tid + 1];
+  const uint32_t v[kPer] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  double m[kPer], tot = 0.0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int b = tid * 8 + j;
-      m += lv.mass(h[b], b);
-    }
-#pragma unroll
-    for (int o = 4; o; o >>= 1) m += __shfl_xor_sync(0xffffffffu, m, o);
-    if ((tid & 7) == 0) ctl.cmass[c] = m;
+  for (int j = 0; j < kPer; ++j) {
+    m[j] = lv.mass(v[j], kPer * tid + j);
+    tot += m[j];
+  }
+  const double inc = warp_incl_f64(tot, lane);
+  if (lane == 31) ctl.red_e[warp] = inc;
+  if (tid == 0) {
+    ctl.misc = INT_MAX;
+    ctl.misc2 = INT_MAX;
   }
   __syncthreads();
-  if (warp == 0) {
-    double cm[2];
+  double run = base + (inc - tot);
+  for (int w = 0; w < warp; ++w) run += ctl.red_e[w];
+  int lo = INT_MAX, hi = INT_MAX;
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) cm[hh] = ctl.cmass[hh * 32 + lane];
-    // first coarse buckets where the upper (slack) and the lower estimate cross
-    int c_lo = -1, c_hi = -1;
-    double run = base, pre_lo = 0.0;
-    for (int hh = 0; hh < 2; ++hh) {
-      const double inc = warp_incl_f64(cm[hh], lane) + run;
-      const uint32_t bl = __ballot_sync(0xffffffffu, topp_crossed(inc * kSlack, z, p));
-      const uint32_t bh = __ballot_sync(0xffffffffu, topp_crossed(inc, z, p));
-      if (c_lo < 0 && bl) {
-        const int l = __ffs(bl) - 1;
-        c_lo = hh * 32 + l;
-        pre_lo = __shfl_sync(0xffffffffu, inc - cm[hh], l);
-      }
-      if (c_hi < 0 && bh) c_hi = hh * 32 + __ffs(bh) - 1;
-      run = __shfl_sync(0xffffffffu, inc, 31);
+  for (int j = 0; j < kPer; ++j) {
+    run += m[j];
+    if (lo == INT_MAX && run * kSlack > thr) lo = kPer * tid + j;
+    if (hi == INT_MAX && run > thr) hi = kPer * tid + j;
+  }
+  if (lo != INT_MAX) atomicMin(&ctl.misc, lo);
+  if (hi != INT_MAX) atomicMin(&ctl.misc2, hi);
+  __syncthreads();
+  const bool found = ctl.misc != INT_MAX;
+  const int fh = ctl.misc2 == INT_MAX ? kBins - 1 : ctl.misc2;
+  const int fl = found ? min(ctl.misc, fh) : 0;
+  // elements in the window ~ mass / smallest value of the bucket
+  double est = 0.0;
+  if (found) {
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int b = kPer * tid + j;
+      const float e_bot = __uint_as_float(lv.lo_key(b));
+      if (b >= fl && b <= fh && m[j] > 0.0 && e_bot > 0.0f) est += (double)__fdividef((float)m[j], e_bot);
     }
-    int found = (c_lo >= 0);
-    int b_lo = 0, b_hi = 0;
-    float est = 0.f;
-    if (found) {
-      if (c_hi < 0) c_hi = kCoarse - 1;
-      double frun = pre_lo;
-      int fl = -1, fh = -1;
-      double est_d = 0.0;
-      for (int c = c_lo; c <= c_hi && fh < 0; ++c) {
-        for (int hh = 0; hh < 2 && fh < 0; ++hh) {
-          const int b = c * kFine + hh * 32 + lane;
-          const double m = lv.mass(h[b], b);
-          const double inc = warp_incl_f64(m, lane) + frun;
-          const uint32_t bl = __ballot_sync(0xffffffffu, topp_crossed(inc * kSlack, z, p));
-          const uint32_t bh = __ballot_sync(0xffffffffu, topp_crossed(inc, z, p));
-          const int flo = (fl < 0 && bl) ? c * kFine + hh * 32 + (__ffs(bl) - 1) : fl;
-          const int fhi = bh ? c * kFine + hh * 32 + (__ffs(bh) - 1) : -1;
-          // elements in the window ~ mass / smallest value of the bucket
-          const bool inwin = (flo >= 0) && b >= flo && (fhi < 0 || b <= fhi);
-          const double e_bot = (double)__uint_as_float(lv.lo_key(b));
-          est_d += warp_dsum((inwin && m > 0.0 && e_bot > 0.0) ? m / e_bot : 0.0);
-          fl = flo;
-          fh = fhi;
-          frun = __shfl_sync(0xffffffffu, inc, 31);
-        }
-      }
-      if (fl < 0) fl = c_lo * kFine;
-      if (fh < 0) fh = c_hi * kFine + kFine - 1;
-      if (fl > fh) fl = fh;
-      b_lo = fl;
-      b_hi = fh;
-      est = (float)(est_d * 1.001 + 1.0);
-    }
-    if (lane == 0) {
-      ctl.sel_found = found;
-      ctl.sel_lo = b_lo;
-      ctl.sel_hi = b_hi;
-      ctl.sel_est = est;
-    }
+  }
+  est = warp_dsum(est);
+  if (lane == 0) ctl.red_e[warp] = est;
+  __syncthreads();
+  if (tid == 0) {
+    double e = 0.0;
+    for (int w = 0; w < kWarps; ++w) e += ctl.red_e[w];
+    ctl.sel_found = found;
+    ctl.sel_lo = found ? fl : 0;
+    ctl.sel_hi = found ? fh : 0;
+    ctl.sel_est = found ? (float)(e * 1.001 + 1.0) : 0.0f;
   }
   __syncthreads();
 }
@@ -1001,8 +993,8 @@ __device__ __forceinline__ void kept_masses(const RowCtx& R, const uint32_t* bit
                                             const typename E::Raw& raw, int idx0, bool valid, float (&q)[E::kEPT]) {
   if (valid) {
     float x[E::kEPT];
-    if (R.pen) penalized<E, true>(bitmap, R.rp, raw, idx0, x);
-    else penalized<E, false>(bitmap, R.rp, raw, idx0, x);
+    if (R.pen) penalized<E, true>(bitmap, R.pp, raw, idx0, x);
+    else penalized<E, false>(bitmap, R.pp, raw, idx0, x);
 #pragma unroll
     for (int j = 0; j < E::kEPT; ++j) {
       const float s = scaled(R, x[j]);
@@ -1151,8 +1143,8 @@ __device__ __forceinline__ int arg_of(const RowCtx& R, const uint32_t* bitmap, c
   const int idx0 = ln.base + bc * E::kPiece;
   const typename E::Raw raw = E::ldg(lane_src<E>(R.src, ln) + bc * kPieceBytes);
   float x[E::kEPT];
-  if (R.pen) penalized<E, true>(bitmap, R.rp, raw, idx0, x);
-  else penalized<E, false>(bitmap, R.rp, raw, idx0, x);
+  if (R.pen) penalized<E, true>(bitmap, R.pp, raw, idx0, x);
+  else penalized<E, false>(bitmap, R.pp, raw, idx0, x);
   int jj = E::kEPT - 1;
 #pragma unroll
   for (int j = E::kEPT - 1; j >= 0; --j)
@@ -1338,6 +1330,230 @@ __device__ __noinline__ double topp_ties(const RowCtx& R, const Sh& sh, Keep& K,
   return zk;
 }
 
+// ---------------------------------------------------------------- top-p members
+// Decision among the window members sh.cand[0, n) (rank keys; every member
+// has bits(e) in [wlo, whi], wlo >= 1): the first member in rank order (value
+// descending, index ascending) whose inclusive mass -- `above` plus the
+// members up to it -- passes thr (topp_threshold of the row total).  Members
+// are grouped by bits(e) into at most kSub sub-buckets whose masses are
+// summed in fixed point (2^-40 of the window top; order-independent), and
+// only the crossing sub-bucket's members are ordered, by one warp.  Returns
+// false, with nothing decided, when that sub-bucket holds more than 32
+// members (the caller then sorts them all).  Otherwise sets ctl.dec_thr /
+// dec_thr_idx to the last kept member, adds the kept members' masses to
+// ctl.seg (per warp range) and ctl.pm (per piece), and returns their total
+// in `kept`.  Uses sh.hist and sh.tm as scratch.  Whole block.
+template <class E>
+__device__ __noinline__ bool member_decide(const Sh sh, int n, uint32_t wlo, uint32_t whi, float m0, double above,
+                                           double thr, int W, double& kept, int tid) {
+  constexpr int kPer = kCandCap / kThreads;
+  Ctl& ctl = *sh.ctl;
+  const int lane = tid & 31, warp = tid >> 5;
+  unsigned long long* sbm = reinterpret_cast<unsigned long long*>(sh.hist);  // [kSub] fixed-point masses
+  uint32_t* sbc = sh.hist + 2 * kSub;                                          // [kSub] counts
+  unsigned long long* small = reinterpret_cast<unsigned long long*>(sh.tm);  // [32] crossing sub-bucket
+  int shs = 0;
+  while (((whi - wlo) >> shs) >= (uint32_t)kSub) ++shs;
+  // F = e * 2^(40 - (E_top - 126)) < 2^41 for every member (E_top: biased exponent of whi)
+  const int etop = (int)(whi >> 23);
+  const double scale = __longlong_as_double((long long)(1023 + 166 - etop) << 52);
+  const double unit = __longlong_as_double((long long)(1023 - 166 + etop) << 52);
+  if (tid < kSub) {
+    sbm[tid] = 0ull;
+    sbc[tid] = 0u;
+  }
+  if (tid == 0) {
+    ctl.misc = INT_MAX;
+    ctl.list_n = 0u;
+    ctl.dec_key = 0ull;
+  }
+  __syncthreads();
+  unsigned long long key[kPer];
+  int sb[kPer];
+  float e[kPer];
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    const int r = tid + q * kThreads;
+    key[q] = ~0ull;
+    sb[q] = -1;
+    e[q] = 0.0f;
+    if (r < n) {
+      key[q] = sh.cand[r];
+      e[q] = exp_shifted(key_value(key[q]), m0);
+      sb[q] = (int)((whi - __float_as_uint(e[q])) >> shs);
+      atomicAdd(&sbc[sb[q]], 1u);
+      atomicAdd(&sbm[sb[q]], (unsigned long long)__double2ull_rz((double)e[q] * scale));
+      atomicMax(&ctl.dec_key, key[q]);  // with no crossing, the last member stays last
+    }
+  }
+  __syncthreads();
+  // the crossing sub-bucket: threads 0..kSub-1 scan the sub-bucket masses
+  double pre = 0.0, m = 0.0;
+  if (tid < kSub) {
+    m = (double)sbm[tid] * unit;
+    const double inc = warp_incl_f64(m, lane);
+    if (lane == 31) ctl.red_e[warp] = inc;
+    pre = inc - m;
+  }
+  __syncthreads();
+  if (tid < kSub) {
+    for (int w = 0; w < warp; ++w) pre += ctl.red_e[w];
+    pre += above;
+    if (sbc[tid] != 0u && pre + m > thr) atomicMin(&ctl.misc, tid);
+  }
+  __syncthreads();
+  const int sbs = ctl.misc;
+  if (tid == sbs) ctl.pick_t = pre;  // mass before the crossing sub-bucket
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    if (sb[q] >= 0 && sb[q] == sbs) {
+      const uint32_t slot = atomicAdd(&ctl.list_n, 1u);
+      if (slot < 32u) small[slot] = key[q];
+    }
+  }
+  __syncthreads();
+  if (sbs != INT_MAX && ctl.list_n > 32u) return false;
+  if (sbs != INT_MAX && warp == 0) {
+    // order the crossing sub-bucket (bitonic across the warp, ascending keys)
+    const int ns = (int)ctl.list_n;
+    unsigned long long k = lane < ns ? small[lane] : ~0ull;
+#pragma unroll
+    for (int kk = 2; kk <= 32; kk <<= 1) {
+#pragma unroll
+      for (int j = kk >> 1; j > 0; j >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, j);
+        const bool take_min = ((lane & j) == 0) == ((lane & kk) == 0);
+        k = take_min ? (k < o ? k : o) : (k < o ? o : k);
+      }
+    }
+    const float ee = lane < ns ? exp_shifted(key_value(k), m0) : 0.0f;
+    const double inc = warp_incl_f64((double)ee, lane) + ctl.pick_t;
+    const uint32_t bal = __ballot_sync(0xffffffffu, lane < ns && inc > thr);
+    const int l = bal ? __ffs(bal) - 1 : ns - 1;
+    const unsigned long long kl = __shfl_sync(0xffffffffu, k, l);
+    if (lane == 0) ctl.dec_key = kl;
+  }
+  __syncthreads();
+  const unsigned long long last = ctl.dec_key;
+  if (tid == 0) {
+    ctl.dec_thr = n > 0 ? key_value(last) : -INFINITY;
+    ctl.dec_thr_idx = n > 0 ? key_index(last) : INT_MAX;
+  }
+  // kept members (rank key <= the last kept one's) join their range and piece masses
+  double lk = 0.0;
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    if (sb[q] >= 0 && key[q] <= last && e[q] > 0.0f) {
+      const int idx = key_index(key[q]);
+      const int w = idx / W;
+      const int c = (idx - w * W) / E::kPiece;
+      atomicAdd(&ctl.seg[w], (double)e[q]);
+      atomicAdd(&ctl.pm[w][c / kStages], (double)e[q]);
+      lk += (double)e[q];
+    }
+  }
+  kept = block_dsum(ctl, lk, tid);  // (its barriers order the mass updates and ctl.dec_*)
+  return true;
+}
+
+// Inverse-CDF draw in vocabulary order from the kept masses per warp range
+// (ctl.seg) and per kStages-chunk piece of it (ctl.pm): warp 0 picks both
+// from shared memory, reads the chosen piece (one round trip) and walks it
+// chunk by chunk.  Falls back to the last kept element when rounding leaves
+// the target past the total, then to `fallback`.  The token is returned in
+// warp 0 (other warps get `fallback`); no barrier.
+template <class E>
+__device__ __noinline__ int draw_piece(const RowCtx R, const Sh sh, const Keep K, double target, int fallback,
+                                       int tid) {
+  if (tid >= 32) return fallback;
+  const Ctl& ctl = *sh.ctl;
+  const int lane = tid;
+  // the warp range
+  const double ms = lane < kWarps ? ctl.seg[lane] : 0.0;
+  const double incs = warp_incl_f64(ms, lane);
+  const uint32_t poss = __ballot_sync(0xffffffffu, ms > 0.0);
+  if (!poss) return fallback;
+  uint32_t hit = __ballot_sync(0xffffffffu, ms > 0.0 && target < incs);
+  int wr;
+  double t1;
+  if (hit) {
+    wr = __ffs(hit) - 1;
+    t1 = target - __shfl_sync(0xffffffffu, incs - ms, wr);
+  } else {
+    wr = 31 - __clz(poss);
+    t1 = 1e300;
+  }
+  // the piece
+  const int np = (R.nch + kStages - 1) / kStages;
+  const double mp = lane < np ? ctl.pm[wr][lane] : 0.0;
+  const double incp = warp_incl_f64(mp, lane);
+  const uint32_t posp = __ballot_sync(0xffffffffu, mp > 0.0);
+  if (!posp) return fallback;
+  hit = __ballot_sync(0xffffffffu, mp > 0.0 && t1 < incp);
+  int pc;
+  double t2;
+  if (hit) {
+    pc = __ffs(hit) - 1;
+    t2 = t1 - __shfl_sync(0xffffffffu, incp - mp, pc);
+  } else {
+    pc = 31 - __clz(posp);
+    t2 = 1e300;
+  }
+  // walk the piece's chunks in vocabulary order
+  constexpr int esz = sizeof(typename E::Raw) / E::kEPT;
+  const int ww = max(0, min(R.W, R.V - wr * R.W));
+  const int c0 = pc * kStages, c1 = min(R.nch, c0 + kStages);
+  const char* base = R.src + (size_t)wr * R.W * esz;
+  typename E::Raw raw[kStages];
+#pragma unroll
+  for (int u = 0; u < kStages; ++u) {
+    const int off = (c0 + u) * E::kPiece + lane * E::kEPT;
+    raw[u] = (c0 + u < c1 && off < ww) ? E::ldg(base + (size_t)off * esz) : E::zero();
+  }
+  int tok = -1, lastk = -1;
+  double run = 0.0;
+#pragma unroll
+  for (int u = 0; u < kStages; ++u) {
+    const int off = (c0 + u) * E::kPiece + lane * E::kEPT;
+    const int idx0 = wr * R.W + off;
+    float q[E::kEPT];
+    kept_masses<E>(R, sh.bitmap, K, raw[u], idx0, c0 + u < c1 && off < ww, q);
+    float ls = 0.f;
+    int lk = -1;
+#pragma unroll
+    for (int j = 0; j < E::kEPT; ++j) {
+      ls = __fadd_rn(ls, q[j]);
+      if (q[j] > 0.f) lk = idx0 + j;
+    }
+    lastk = max(lastk, (int)__reduce_max_sync(0xffffffffu, (uint32_t)(lk + 1)) - 1);
+    const double inc = warp_incl_f64((double)ls, lane) + run;
+    const uint32_t bal = __ballot_sync(0xffffffffu, inc > t2 && ls > 0.f);
+    if (bal) {
+      const int l = __ffs(bal) - 1;
+      int mine = -1;
+      if (lane == l) {
+        double cum = inc - (double)ls;
+        int pk = -1, lastc = -1;
+#pragma unroll
+        for (int j = 0; j < E::kEPT; ++j) {
+          if (q[j] > 0.f) {
+            lastc = j;
+            cum += (double)q[j];
+            if (pk < 0 && cum > t2) pk = j;
+          }
+        }
+        if (pk < 0) pk = lastc;
+        mine = idx0 + pk;
+      }
+      tok = __shfl_sync(0xffffffffu, mine, l);
+      break;
+    }
+    run = __shfl_sync(0xffffffffu, inc, 31);
+  }
+  if (tok < 0) tok = lastk >= 0 ? lastk : fallback;
+  return tok;
+}
+
 // ---------------------------------------------------------------- top-k lists
 // One chunk's logits of a thread, passed by value to out-of-line helpers.
 template <class E>
@@ -1393,6 +1609,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
   R.p = P.top_p;
   R.k = (P.top_k > 0 && P.top_k < V) ? P.top_k : 0;
   R.rp = P.repetition_penalty;
+  R.pp = Pen{R.rp, __frcp_rn(R.rp)};
   const int64_t h0 = in.h[0], h1 = in.h[1];
   R.pen = (P.flags & NS_ROW_PENALTY) != 0u && a.history_offsets && h1 > h0;
   const bool ring2 = ctl.plan[i & 1].passes == 2;
@@ -1437,8 +1654,8 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
   RingWalk rw(sh, ln, fd1, stage);
   // chunks [c0, c1) of this row's first pass, specialised on whether the penalty is on
   auto first_range = [&](int c0, int c1, auto&& body) {
-    if (R.pen) ring_range<E, true>(sh, ln, fd1, rw, c0, c1, nch, R.rp, body);
-    else ring_range<E, false>(sh, ln, fd1, rw, c0, c1, nch, R.rp, body);
+    if (R.pen) ring_range<E, true>(sh, ln, fd1, rw, c0, c1, nch, R.pp, body);
+    else ring_range<E, false>(sh, ln, fd1, rw, c0, c1, nch, R.pp, body);
   };
 
   // ================================================================ first pass
@@ -1466,7 +1683,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
     S = block_stats(ctl, st, arg_of<E>(R, sh.bitmap, ln, best, best_c), 0.0, 0u, tid);
   } else if (mode == kTopk) {
     // the bound from chunk 0's thread maxima, refreshed after chunk kRefreshAt
-    float tmax = peek_max<E>(sh, ln, stage, R.pen, R.rp);
+    float tmax = peek_max<E>(sh, ln, stage, R.pen, R.pp);
     tau = topk_bound(R.k, R.t_one, R.T, R.rT, &ctl, sh.tm, tmax, tid);
     // each warp appends to its own list (slots counted in a warp-uniform register)
     unsigned long long* wl = sh.cand + warp * kWarpCands;
@@ -1501,7 +1718,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
     double lz = 0.0;
     const bool with_e = R.k == 0;  // large top-k computes its masses after the select
     if (with_e) {
-      const float pm = peek_max<E>(sh, ln, stage, R.pen, R.rp);
+      const float pm = peek_max<E>(sh, ln, stage, R.pen, R.pp);
       const uint32_t wk = __reduce_max_sync(0xffffffffu, pm != pm ? 0u : f2key(pm));
       if (lane == 0) ctl.red_b[warp] = wk;
       __syncthreads();
@@ -1772,13 +1989,14 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
 
   double zk = z;
   bool ring_used = false;
+  bool pm_ok = false;  // ctl.pm holds the kept masses per draw piece
   if (R.topp) {
-    topp_window(&ctl, sh.hist, lv, 0.0, z, R.p, tid);
+    topp_window(&ctl, sh.hist, lv, 0.0, topp_threshold(z, R.p), tid);
     if (!ctl.sel_found && lumped) {
       // the boundary may lie among masses below the level: locate it on the wide one
       lv = Level{kTopWide, kShWide, true};
       stats_pass(lv, true);
-      topp_window(&ctl, sh.hist, lv, 0.0, z, R.p, tid);
+      topp_window(&ctl, sh.hist, lv, 0.0, topp_threshold(z, R.p), tid);
     }
     const bool crossed = ctl.sel_found != 0;
     uint32_t win_lo = 0u, win_hi = 0u;
@@ -1821,7 +2039,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
         });
         const double above_lv = block_dsum(ctl, la, tid);
         const Level lv2{win_hi, sh2, false};
-        topp_window(&ctl, sh.hist, lv2, above_lv, z, R.p, tid);
+        topp_window(&ctl, sh.hist, lv2, above_lv, topp_threshold(z, R.p), tid);
         if (ctl.sel_found) {
           lv = lv2;
           win_lo = lv.lo_key(ctl.sel_hi);
@@ -1838,43 +2056,59 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       double la = 0.0;
       const Keep K1 = K;
       const uint32_t wlo = max(win_lo, 1u), whi = win_hi;
-      auto collect = [&](int, const float(&x)[EPT], int idx0, bool live) {
-        if (!live) return;
-        float s[EPT];
-        if (R.t_one) {
-#pragma unroll
-          for (int j = 0; j < EPT; ++j) s[j] = x[j];
-        } else {
-#pragma unroll
-          for (int j = 0; j < EPT; ++j) s[j] = div_by_const(x[j], R.T, R.rT);
+      // per-thread mass above the window in the current draw piece (kStages
+      // chunks; chunks are visited in order from 0, the same in every lane)
+      float pacc = 0.0f;
+      int pleft = kStages, pidx = 0;
+      auto piece_end = [&](int c, float part) {
+        pacc = __fadd_rn(pacc, part);
+        if (--pleft == 0 || c == nch - 1) {
+          const double ps = warp_dsum((double)pacc);
+          if (lane == 0) ctl.pm[warp][pidx] = ps;
+          pacc = 0.0f;
+          pleft = kStages;
+          ++pidx;
         }
+      };
+      auto collect = [&](int c, const float(&x)[EPT], int idx0, bool live) {
         float part = 0.0f;
-        bool anym = false;
-        uint32_t bits[EPT];
+        if (live) {
+          float s[EPT];
+          if (R.t_one) {
 #pragma unroll
-        for (int j = 0; j < EPT; ++j) {
-          const float e = K1.mass(s[j]);
-          bits[j] = __float_as_uint(e);
-          if (bits[j] > whi) part = __fadd_rn(part, e);
-          anym |= (bits[j] >= wlo && bits[j] <= whi);
-        }
-        la += (double)part;
-        if (anym) {
-          // rare: append this thread's window members one by one
+            for (int j = 0; j < EPT; ++j) s[j] = x[j];
+          } else {
+#pragma unroll
+            for (int j = 0; j < EPT; ++j) s[j] = div_by_const(x[j], R.T, R.rT);
+          }
+          bool anym = false;
+          uint32_t bits[EPT];
 #pragma unroll
           for (int j = 0; j < EPT; ++j) {
-            if (bits[j] >= wlo && bits[j] <= whi) {
-              const uint32_t slot = atomicAdd(&ctl.cand_n, 1u);
-              if (slot < (uint32_t)kCandCap) sh.cand[slot] = rank_key(s[j], idx0 + j);
+            const float e = K1.mass(s[j]);
+            bits[j] = __float_as_uint(e);
+            if (bits[j] > whi) part = __fadd_rn(part, e);
+            anym |= (bits[j] >= wlo && bits[j] <= whi);
+          }
+          if (anym) {
+            // rare: append this thread's window members one by one
+#pragma unroll
+            for (int j = 0; j < EPT; ++j) {
+              if (bits[j] >= wlo && bits[j] <= whi) {
+                const uint32_t slot = atomicAdd(&ctl.cand_n, 1u);
+                if (slot < (uint32_t)kCandCap) sh.cand[slot] = rank_key(s[j], idx0 + j);
+              }
             }
           }
         }
+        la += (double)part;
+        piece_end(c, part);
       };
       if (ring2 && !ring_used && !K.have_k) {
         ring_used = true;
         const Feed fd2 = feed_second<E>(ctl, i, ln, true);
         const float mm = m0;
-        auto collect_ring = [&](int, const float(&x)[EPT], int idx0, bool) {
+        auto collect_ring = [&](int c, const float(&x)[EPT], int idx0, bool) {
           float s[EPT];
           if (R.t_one) {
 #pragma unroll
@@ -1903,9 +2137,10 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
               }
             }
           }
+          piece_end(c, part);
         };
-        if (R.pen) ring_pass<E, true>(sh, ln, fd2, nch, stage, R.rp, collect_ring);
-        else ring_pass<E, false>(sh, ln, fd2, nch, stage, R.rp, collect_ring);
+        if (R.pen) ring_pass<E, true>(sh, ln, fd2, nch, stage, R.pp, collect_ring);
+        else ring_pass<E, false>(sh, ln, fd2, nch, stage, R.pp, collect_ring);
       } else {
         global_pass<E>(R, sh.bitmap, tid, collect);
       }
@@ -1920,9 +2155,23 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
         zk = topp_ties<E>(R, sh, K, max(win_lo, 1u), win_hi, above, z, status, tid);
         break;
       }
+      const int n = (int)min(ntot, (uint32_t)kCandCap);
+      if (ntot <= (uint32_t)kCandCap) {
+        // ---- decision by sub-buckets of the members (the usual case)
+        double kept_m = 0.0;
+        if (member_decide<E>(sh, n, max(win_lo, 1u), win_hi, m0, above, topp_threshold(z, R.p), W, kept_m, tid)) {
+          zk = above + kept_m;
+          pm_ok = true;
+          K.window = true;
+          K.win_lo = win_lo;
+          K.win_hi = win_hi;
+          K.thr = ctl.dec_thr;
+          K.thr_idx = ctl.dec_thr_idx;
+          break;
+        }
+      }
       // ---- decision on the sorted window members: the first rank whose
       // inclusive mass crosses (block-wide scan, 4 ranks per thread)
-      const int n = (int)min(ntot, (uint32_t)kCandCap);
       if (ntot > (uint32_t)kCandCap && tid == 0 && status) atomicOr(status, NS_STATUS_CAP_OVERFLOW);
       sort_keys(sh.cand, n, tid);
       if (tid == 0) ctl.misc = INT_MAX;
@@ -1964,11 +2213,14 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       for (int q = 0; q < 4; ++q) {
         const int r = 4 * tid + q;
         if (r <= j0 && er[q] > 0.0f) {
-          atomicAdd(&ctl.seg[key_index(sh.cand[r]) / W], (double)er[q]);
+          const int idx = key_index(sh.cand[r]);
+          atomicAdd(&ctl.seg[idx / W], (double)er[q]);
+          atomicAdd(&ctl.pm[idx / W][(idx % W) / E::kPiece / kStages], (double)er[q]);
           lk += (double)er[q];
         }
       }
       zk = above + block_dsum(ctl, lk, tid);  // (its barriers order the range updates)
+      pm_ok = ntot <= (uint32_t)kCandCap;
       K.window = true;
       K.win_lo = win_lo;
       K.win_hi = win_hi;
@@ -1990,8 +2242,8 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       if (ring2 && !ring_used) {
         ring_used = true;
         const Feed fd2 = feed_second<E>(ctl, i, ln, true);
-        if (R.pen) ring_pass<E, true>(sh, ln, fd2, nch, stage, R.rp, plain);
-        else ring_pass<E, false>(sh, ln, fd2, nch, stage, R.rp, plain);
+        if (R.pen) ring_pass<E, true>(sh, ln, fd2, nch, stage, R.pp, plain);
+        else ring_pass<E, false>(sh, ln, fd2, nch, stage, R.pp, plain);
       } else {
         global_pass<E>(R, sh.bitmap, tid, plain);
       }
@@ -2001,7 +2253,9 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
   if (ring2 && !ring_used) stage = drain_pass(sh.ring, feed_second<E>(ctl, i, ln, false), ln, nch, stage, E::kNegInf2);
 
   // ---- the draw
-  const int tok = R.greedy ? S.arg : draw_token<E>(R, sh, K, u * zk, S.arg, tid);
+  const int tok = R.greedy ? S.arg
+                 : pm_ok   ? draw_piece<E>(R, sh, K, u * zk, S.arg, tid)
+                           : draw_token<E>(R, sh, K, u * zk, S.arg, tid);
   if (tid == 0) write_token(a.out_tokens, out_i32, row, tok == INT_MAX ? 0 : tok);
   if (debug) {
     global_pass<E>(R, sh.bitmap, tid, [&](int, const float(&x)[EPT], int idx0, bool live) {
