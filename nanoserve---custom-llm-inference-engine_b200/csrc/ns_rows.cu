@@ -48,6 +48,7 @@
 
 #include <climits>
 #include <mutex>
+#include <cstdlib>
 #include <string>
 
 #include "../../include/nanoserve_sampler.h"
@@ -171,6 +172,7 @@ struct RowPlan {
   const char* src;  // the row in global memory
   int passes;       // passes through the ring (1, or 2 for top-p rows)
   int valid;        // the row exists
+  int pre;          // the pre-pass has streamed its first pass
 };
 
 struct __align__(16) Ctl {
@@ -550,9 +552,40 @@ __device__ __forceinline__ void fetch_row_inputs(const NsSampleArgs& a, RowIn& d
   reinterpret_cast<uint4*>(&dst)[tid] = v;
 }
 
+// ---------------------------------------------------------------- pre-pass
+// The first pass of top-p rows without top-k, split over kPreParts blocks per
+// row and run as its own kernel ahead of the row kernel (same stream): each
+// block streams one contiguous part of the row and leaves the part's
+// locator histogram and statistics in g_pre_*; the row kernel adds the parts
+// and goes straight to the top-p window, so such a row streams through its
+// own block once instead of twice.  Every part uses the row kernel's m0 (the
+// maximum of the row's first chunk, which every part reads), so the parts'
+// histograms add up exactly to the one the row kernel would have built.
+constexpr int kPreRows = 256;  // calls with at most this many rows use the pre-pass
+constexpr int kPreParts = 4;   // blocks per row
+
+struct PreStats {
+  double z;        // sum over the part of e = exp(s - m0)
+  uint32_t mxkey;  // orderable key of the part's largest penalized logit (0xffffffff: a NaN)
+  float m0;
+  uint32_t pad[2];
+};
+
+// Scratch of the pre-pass (device globals, no allocation): slot r belongs to
+// row r of the current call.  Calls that overlap on the GPU race on it.
+__device__ uint32_t g_pre_hist[kPreRows][kPreParts][kBins];
+__device__ PreStats g_pre_stats[kPreRows][kPreParts];
+
+// Rows the pre-pass serves: top-p on, top-k off, no debug outputs.
+__device__ __forceinline__ bool pre_row(const NsRowParams& P, int V, bool debug) {
+  const bool k_on = P.top_k > 0 && P.top_k < V;
+  return !debug && (P.flags & NS_ROW_GREEDY) == 0u && (P.flags & NS_ROW_TOP_P) != 0u && !k_on;
+}
+
 // Plan of this block's i-th row (taken at position `ticket` of the row
 // order), from its fetched inputs.
-__device__ __forceinline__ void make_plan(const NsSampleArgs& a, Ctl& ctl, int i, int ticket, bool debug) {
+__device__ __forceinline__ void make_plan(const NsSampleArgs& a, Ctl& ctl, int i, int ticket, bool debug,
+                                          bool pre_on) {
   RowPlan& pl = ctl.plan[i & 1];
   if (ticket >= a.num_rows) {
     pl.valid = 0;
@@ -564,7 +597,8 @@ __device__ __forceinline__ void make_plan(const NsSampleArgs& a, Ctl& ctl, int i
   const size_t esize = a.logits_dtype == NS_DTYPE_BF16 ? 2 : 4;
   pl.src = static_cast<const char*>(a.logits) + (size_t)src * (size_t)a.logits_row_stride * esize;
   const int mode = row_mode(in.P, a.vocab_size, debug);
-  pl.passes = (mode == kGeneral && (in.P.flags & NS_ROW_TOP_P)) ? 2 : 1;
+  pl.pre = (pre_on && in.row < kPreRows && pre_row(in.P, a.vocab_size, debug)) ? 1 : 0;
+  pl.passes = (!pl.pre && mode == kGeneral && (in.P.flags & NS_ROW_TOP_P)) ? 2 : 1;
   pl.valid = 1;
 }
 
@@ -1582,6 +1616,132 @@ __device__ __noinline__ int topk_insert(unsigned long long* wl, int wcnt, const 
   return wcnt;
 }
 
+// ---------------------------------------------------------------- pre-pass kernel
+template <class E>
+__global__ void __launch_bounds__(kThreads) pre_kernel(const NsSampleArgs a, int W) {
+  constexpr int EPT = E::kEPT;
+  constexpr int esz = sizeof(typename E::Raw) / EPT;
+  __shared__ __align__(16) uint32_t hist[kBins];
+  __shared__ uint32_t bitmap[(kMaxVocab + 31) / 32];
+  __shared__ uint32_t red_k[kWarps];
+  __shared__ double red_z[kWarps];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row = blockIdx.x / kPreParts, part = blockIdx.x % kPreParts;
+  if (row >= a.num_rows) return;
+  const NsRowParams P = a.row_params[row];
+  const int V = a.vocab_size;
+  const bool debug = (a.out_filtered != nullptr) || (a.out_probs != nullptr);
+  if (!pre_row(P, V, debug)) return;
+  int64_t src = a.sample_indices ? a.sample_indices[row] : row;
+  if (src < 0 || src >= a.num_logit_rows) src = 0;  // the row kernel reports it
+  const char* rs = static_cast<const char*>(a.logits) + (size_t)src * (size_t)a.logits_row_stride * esz;
+  const float T = P.temperature;
+  const float rT = __frcp_rn(T);
+  const bool t_one = (T == 1.0f);
+  const int64_t h0 = a.history_offsets ? a.history_offsets[row] : 0;
+  const int64_t h1 = a.history_offsets ? a.history_offsets[row + 1] : 0;
+  const bool pen = (P.flags & NS_ROW_PENALTY) != 0u && a.history_offsets && h1 > h0;
+  const Pen pp{P.repetition_penalty, __frcp_rn(P.repetition_penalty)};
+
+  for (int b = tid; b < kBins / 4; b += kThreads) reinterpret_cast<uint4*>(hist)[b] = make_uint4(0, 0, 0, 0);
+  if (pen)
+    for (int w = tid; w < (V + 31) / 32; w += kThreads) bitmap[w] = 0u;
+  __syncthreads();
+  if (pen) {
+    for (int64_t h = h0 + tid; h < h1; h += kThreads) {
+      const int id = a.history_ids[h];
+      if (id >= 0 && id < V) atomicOr(&bitmap[id >> 5], 1u << (id & 31));
+    }
+  }
+  __syncthreads();
+  // m0: the row kernel's first chunk (thread t: warp range t / 32, its lane's 16 bytes)
+  float pm = -INFINITY;
+  {
+    const int ww = max(0, min(W, V - warp * W));
+    const int idx0 = warp * W + lane * EPT;
+    if (lane * EPT < ww) {
+      float x[EPT];
+      const typename E::Raw raw = E::ldg(rs + (size_t)idx0 * esz);
+      if (pen) penalized<E, true>(bitmap, pp, raw, idx0, x);
+      else penalized<E, false>(bitmap, pp, raw, idx0, x);
+      pm = x[0];
+#pragma unroll
+      for (int j = 1; j < EPT; ++j) pm = fmax_nan(pm, x[j]);
+    }
+  }
+  {
+    const uint32_t wk = __reduce_max_sync(0xffffffffu, pm != pm ? 0u : f2key(pm));
+    if (lane == 0) red_k[warp] = wk;
+  }
+  __syncthreads();
+  uint32_t ck = 0u;
+  for (int w = 0; w < kWarps; ++w) ck = max(ck, red_k[w]);
+  const float mx0 = key2f(ck);
+  const float m0 = (mx0 > -INFINITY && mx0 < INFINITY) ? (t_one ? mx0 : div_by_const(mx0, T, rT)) : 0.0f;
+  __syncthreads();  // red_k is reused below
+  // this part's 16-byte slots, block-strided
+  const int nslots = V / EPT;
+  const int s_lo = (int)((int64_t)part * nslots / kPreParts), s_hi = (int)((int64_t)(part + 1) * nslots / kPreParts);
+  float lmax = -INFINITY;
+  double lz = 0.0;
+  constexpr int U = 4;
+  for (int s0 = s_lo + tid; s0 < s_hi; s0 += U * kThreads) {
+    typename E::Raw raw[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int sl = s0 + u * kThreads;
+      raw[u] = sl < s_hi ? E::ldg(rs + (size_t)sl * sizeof(typename E::Raw)) : E::zero();
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int sl = s0 + u * kThreads;
+      if (sl >= s_hi) continue;
+      float x[EPT];
+      if (pen) penalized<E, true>(bitmap, pp, raw[u], sl * EPT, x);
+      else penalized<E, false>(bitmap, pp, raw[u], sl * EPT, x);
+      float part_z = 0.0f;
+#pragma unroll
+      for (int j = 0; j < EPT; ++j) {
+        lmax = fmax_nan(lmax, x[j]);
+        const float s = t_one ? x[j] : div_by_const(x[j], T, rT);
+        const float e = exp_shifted(s, m0);
+        part_z = __fadd_rn(part_z, e);
+        const uint32_t bits = __float_as_uint(e);
+        atomicAdd(&hist[min((kTopFine - bits) >> kShFine, (uint32_t)(kBins - 1))], approx_mass13(bits));
+      }
+      lz += (double)part_z;
+    }
+  }
+  {
+    const bool nan = (lmax != lmax);
+    const uint32_t wk = __reduce_max_sync(0xffffffffu, nan ? 0u : f2key(lmax));
+    const bool wn = __any_sync(0xffffffffu, nan);
+    const double wz = warp_dsum(lz);
+    if (lane == 0) {
+      red_k[warp] = wn ? 0xffffffffu : wk;
+      red_z[warp] = wz;
+    }
+  }
+  __syncthreads();
+  uint32_t* gh = g_pre_hist[row][part];
+  for (int b = tid; b < kBins / 4; b += kThreads)
+    reinterpret_cast<uint4*>(gh)[b] = reinterpret_cast<const uint4*>(hist)[b];
+  if (tid == 0) {
+    uint32_t k = 0u;
+    double z = 0.0;
+    for (int w = 0; w < kWarps; ++w) {
+      k = max(k, red_k[w]);
+      z += red_z[w];
+    }
+    PreStats st;
+    st.z = z;
+    st.mxkey = k;
+    st.m0 = m0;
+    st.pad[0] = st.pad[1] = 0u;
+    g_pre_stats[row][part] = st;
+  }
+}
+
 // ---------------------------------------------------------------- one row
 template <class E>
 __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, const Lane& ln, int& stage, int i,
@@ -1613,6 +1773,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
   const int64_t h0 = in.h[0], h1 = in.h[1];
   R.pen = (P.flags & NS_ROW_PENALTY) != 0u && a.history_offsets && h1 > h0;
   const bool ring2 = ctl.plan[i & 1].passes == 2;
+  const bool pre = ctl.plan[i & 1].pre != 0;  // first pass done by the pre-pass; the ring has the second
   int mode = row_mode(P, V, debug);
   const int64_t out_off = (int64_t)row * V;
 
@@ -1668,6 +1829,41 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
   // was first seen in; the element index is recovered after the pass
   float best = -INFINITY;
   int best_c = -1;
+  if (pre) {
+    // the pre-pass streamed this row: add its parts' histograms and statistics
+    const uint4* gh = reinterpret_cast<const uint4*>(&g_pre_hist[row][0][0]);
+    for (int b = tid; b < kBins / 4; b += kThreads) {
+      uint4 acc = gh[b];
+#pragma unroll
+      for (int q = 1; q < kPreParts; ++q) {
+        const uint4 v = gh[q * (kBins / 4) + b];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      reinterpret_cast<uint4*>(sh.hist)[b] = acc;
+    }
+    uint32_t key = 0u;
+    double zz = 0.0;
+#pragma unroll
+    for (int q = 0; q < kPreParts; ++q) {
+      key = max(key, g_pre_stats[row][q].mxkey);
+      zz += g_pre_stats[row][q].z;
+    }
+    m0 = g_pre_stats[row][0].m0;
+    S.nan = (key == 0xffffffffu);
+    S.mx = S.nan ? __int_as_float(0x7fc00000) : key2f(key);
+    S.arg = INT_MAX;
+    S.z = zz;
+    S.over = false;
+    S.lumped = false;
+    __syncthreads();
+    if (!(S.nan || S.mx == INFINITY || S.mx == -INFINITY)) {
+      over = __float_as_uint(exp_shifted(scaled(R, S.mx), m0)) > kTopFine;
+      lumped = (sh.hist[kBins - 1] != 0u) ? 1u : 0u;
+    }
+  } else {
   if (mode == kGreedy) {
     float st = -INFINITY;
     first_range(0, nch, [&](int c, const float(&x)[EPT], int, bool) {
@@ -1765,6 +1961,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
     }
   }
   stage = (stage + nch) % kStages;
+  }
 
   if (a.out_penalized) {
     // debug output: the logits after the repetition penalty (sampler.py:31-38)
@@ -1779,7 +1976,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
   // ================================================================ rows whose softmax is NaN
   // NaN or +inf logits, or all -inf: uniform probabilities 1/V (sampler.py:76-80)
   if (S.nan || S.mx == INFINITY || S.mx == -INFINITY) {
-    if (ring2) stage = drain_pass(sh.ring, feed_second<E>(ctl, i, ln, false), ln, nch, stage, E::kNegInf2);
+    if (ring2 || pre) stage = drain_pass(sh.ring, feed_second<E>(ctl, i, ln, false), ln, nch, stage, E::kNegInf2);
     int tok;
     if (R.greedy) {
       // torch.argmax: the first NaN, else the first +inf, else index 0.  The
@@ -2104,9 +2301,9 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
         la += (double)part;
         piece_end(c, part);
       };
-      if (ring2 && !ring_used && !K.have_k) {
+      if ((ring2 || pre) && !ring_used && !K.have_k) {
         ring_used = true;
-        const Feed fd2 = feed_second<E>(ctl, i, ln, true);
+        const Feed fd2 = pre ? fd1 : feed_second<E>(ctl, i, ln, true);
         const float mm = m0;
         auto collect_ring = [&](int c, const float(&x)[EPT], int idx0, bool) {
           float s[EPT];
@@ -2239,9 +2436,9 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
         for (int j = 0; j < EPT; ++j) part = __fadd_rn(part, K1.mass(scaled(R, x[j])));
         lz += (double)part;
       };
-      if (ring2 && !ring_used) {
+      if ((ring2 || pre) && !ring_used) {
         ring_used = true;
-        const Feed fd2 = feed_second<E>(ctl, i, ln, true);
+        const Feed fd2 = pre ? fd1 : feed_second<E>(ctl, i, ln, true);
         if (R.pen) ring_pass<E, true>(sh, ln, fd2, nch, stage, R.pp, plain);
         else ring_pass<E, false>(sh, ln, fd2, nch, stage, R.pp, plain);
       } else {
@@ -2250,7 +2447,8 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
       zk = block_segments(ctl, lz, tid);
     }
   }
-  if (ring2 && !ring_used) stage = drain_pass(sh.ring, feed_second<E>(ctl, i, ln, false), ln, nch, stage, E::kNegInf2);
+  if ((ring2 || pre) && !ring_used)
+    stage = drain_pass(sh.ring, feed_second<E>(ctl, i, ln, false), ln, nch, stage, E::kNegInf2);
 
   // ---- the draw
   const int tok = R.greedy ? S.arg
@@ -2274,7 +2472,7 @@ __device__ __forceinline__ void sample_row(const NsSampleArgs& a, const Sh& sh, 
 
 // ---------------------------------------------------------------- the kernel
 template <class E>
-__global__ void __launch_bounds__(kThreads, 2) row_kernel(const NsSampleArgs a, int W, int nch) {
+__global__ void __launch_bounds__(kThreads, 2) row_kernel(const NsSampleArgs a, int W, int nch, int pre_on) {
   extern __shared__ __align__(128) unsigned char smem[];
   const Layout L = make_layout(a.vocab_size);
   Sh sh;
@@ -2294,13 +2492,13 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const NsSampleArgs a, 
   if (t0 < a.num_rows) fetch_row_inputs(a, ctl.rin[0], t0, tid);
   if (t0 + G < a.num_rows) fetch_row_inputs(a, ctl.rin[1], t0 + G, tid);
   __syncthreads();
-  if (tid == 0) make_plan(a, ctl, 0, t0, debug);
+  if (tid == 0) make_plan(a, ctl, 0, t0, debug, pre_on != 0);
   __syncthreads();
   ring_start<E>(ctl, sh.ring, ln);
   int stage = 0;
   for (int i = 0, t = t0; t < a.num_rows; ++i, t += G) {
     __syncthreads();  // the previous row is finished; row i+1's inputs are in place
-    if (tid == 0) make_plan(a, ctl, i + 1, t + G, debug);
+    if (tid == 0) make_plan(a, ctl, i + 1, t + G, debug, pre_on != 0);
     if (t + 2 * G < a.num_rows) fetch_row_inputs(a, ctl.rin[(i + 2) & 3], t + 2 * G, tid);
     sample_row<E>(a, sh, ln, stage, i, (int)ctl.rin[i & 3].row, nch, W);
   }
@@ -2377,7 +2575,23 @@ int rows_launch(const NsSampleArgs& a, cudaStream_t stream, int device, std::str
   }
   const int cap = per_sm * sms;
   const int grid = a.num_rows < cap ? a.num_rows : cap;
-  void* args[] = {const_cast<NsSampleArgs*>(&a), const_cast<int*>(&W), const_cast<int*>(&nch)};
+  // top-p rows of small batches: their first pass runs split over several
+  // blocks per row first (same stream), the row kernel picks it up
+  const bool debug = a.out_filtered != nullptr || a.out_probs != nullptr;
+  const char* pe_env = std::getenv("NS_PREPASS");  // "0": every row streams in its own block
+  int pre_on = (!debug && a.num_rows <= kPreRows && !(pe_env && pe_env[0] == '0')) ? 1 : 0;
+  if (pre_on) {
+    const void* pfn = bf16 ? reinterpret_cast<const void*>(&pre_kernel<EBF16>)
+                           : reinterpret_cast<const void*>(&pre_kernel<EF32>);
+    void* pargs[] = {const_cast<NsSampleArgs*>(&a), const_cast<int*>(&W)};
+    const cudaError_t pe =
+        cudaLaunchKernel(pfn, dim3((unsigned)(a.num_rows * kPreParts)), dim3(kThreads), pargs, 0, stream);
+    if (pe != cudaSuccess) {
+      err = std::string("pre-pass launch: ") + cudaGetErrorString(pe);
+      return NS_ERR_CUDA;
+    }
+  }
+  void* args[] = {const_cast<NsSampleArgs*>(&a), const_cast<int*>(&W), const_cast<int*>(&nch), &pre_on};
   const cudaError_t e = cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kThreads), args, L.total, stream);
   if (e != cudaSuccess) {
     err = std::string("row kernel launch: ") + cudaGetErrorString(e);

@@ -264,3 +264,33 @@ def test_row_order_changes_nothing_but_the_schedule():
                      row_order=torch.from_numpy(bad).to(dev))
     assert got["status"] == H.cabi.NS_STATUS_BAD_ROW_ORDER
     assert np.array_equal(got["tokens"], base["tokens"])
+
+
+@pytest.mark.parametrize("prepass", ["1", "0"])
+@pytest.mark.parametrize("V", [32768, 128256])
+def test_top_p_rows_without_debug_outputs(V, prepass, monkeypatch):
+    """The production path (no debug outputs): top-p rows may stream their
+    first pass through the split pre-pass, which must give the oracle's
+    tokens like the single-block path does (NS_PREPASS=0)."""
+    monkeypatch.setenv("NS_PREPASS", prepass)
+    dev = _dev()
+    rng = np.random.default_rng(44)
+    SP = importlib.import_module(H.PKG + ".config").SamplingParams
+    rows, params, hists = [], [], []
+    kinds = [SP(temperature=1.0, top_p=0.9), SP(temperature=0.7, top_p=0.9, repetition_penalty=1.2),
+             SP(temperature=1.3, top_p=0.99), SP(temperature=0.0), SP(temperature=1.0, top_k=50),
+             SP(temperature=1.0, top_p=0.5), SP(temperature=0.9, top_p=0.95, repetition_penalty=0.8)]
+    for r in range(48):
+        p = kinds[r % len(kinds)]
+        flat = r % len(kinds) == 2
+        x = (rng.standard_normal(V) * (0.5 if flat else 2.0)).astype(np.float32)
+        if not flat:
+            x[rng.integers(0, V, 20)] += 8.0
+        rows.append(x)
+        params.append(p)
+        hists.append(rng.integers(0, V, 700).tolist() if p.repetition_penalty != 1.0 else [])
+    lg = torch.from_numpy(np.stack(rows)).to(dev)
+    u = rng.random(len(rows)).astype(np.float32)
+    gpu = H.run_cabi(lg, params, hists, u, debug=False)
+    assert gpu["status"] == 0
+    _check(H.compare(gpu, np.stack(rows), params, hists, u))
