@@ -142,6 +142,25 @@ typedef struct NsSampleArgs {
  * allocation.  Replaces sampler.py:21-89 (Sampler.sample). */
 int ns_sample(const NsSampleArgs* args, void* stream);
 
+/* Largest num_rows that ns_sample_noalloc accepts. */
+#define NS_NOALLOC_MAX_ROWS 256
+
+/* ns_sample for callers that must not allocate device memory: an engine that
+ * reserves all of the GPU's memory for its own pool at start-up and makes no
+ * cudaMalloc afterwards, or a host that embeds this library under a strict
+ * memory budget.  It allocates nothing on any call.  Every scratch buffer it
+ * needs is a file-scope static device array of the library (16 MB, room for
+ * NS_NOALLOC_MAX_ROWS rows), which every GPU that loads the library holds
+ * until the process exits.  Calls with more rows return NS_ERR_UNSUPPORTED
+ * (ns_sample serves them).  The first call on each device looks up the
+ * array's device address once, so make that first call outside any stream
+ * capture.  Every call shares the array, ns_sample's calls included; nothing
+ * in it needs to start at zero, but calls that overlap on the GPU (different
+ * streams, or several host threads at once) race on it.  Same arguments and
+ * same outputs as ns_sample.  No counterpart in the reference
+ * (nanoserve/scheduler/sampler.py allocates through torch). */
+int ns_sample_noalloc(const NsSampleArgs* args, void* stream);
+
 /* Message for the last non-OK status returned on this host thread. */
 const char* ns_last_error(void);
 

@@ -36,7 +36,8 @@ NS_STATUS_CAP_OVERFLOW = 0x8
 NS_STATUS_BAD_ROW_ORDER = 0x10
 
 # every entry point the header declares
-EXPORTED_SYMBOLS = ("ns_sample", "ns_last_error", "ns_abi_version", "ns_max_vocab")
+EXPORTED_SYMBOLS = ("ns_sample", "ns_sample_noalloc", "ns_last_error", "ns_abi_version", "ns_max_vocab")
+NS_NOALLOC_MAX_ROWS = 256
 
 
 class NsRowParams(ctypes.Structure):
@@ -98,6 +99,8 @@ def load_library() -> ctypes.CDLL:
         lib = ctypes.CDLL(str(LIB_PATH))
         lib.ns_sample.argtypes = [ctypes.POINTER(NsSampleArgs), ctypes.c_void_p]
         lib.ns_sample.restype = ctypes.c_int
+        lib.ns_sample_noalloc.argtypes = [ctypes.POINTER(NsSampleArgs), ctypes.c_void_p]
+        lib.ns_sample_noalloc.restype = ctypes.c_int
         lib.ns_last_error.argtypes = []
         lib.ns_last_error.restype = ctypes.c_char_p
         lib.ns_abi_version.argtypes = []
@@ -117,5 +120,14 @@ class NsError(RuntimeError):
 def ns_sample(args: NsSampleArgs, stream: int = 0) -> None:
     lib = load_library()
     rc = lib.ns_sample(ctypes.byref(args), ctypes.c_void_p(stream))
+    if rc != NS_OK:
+        raise NsError(rc, lib.ns_last_error().decode(errors="replace"))
+
+
+def ns_sample_noalloc(args: NsSampleArgs, stream: int = 0) -> None:
+    """The entry point for callers that cannot allocate device memory (at most
+    NS_NOALLOC_MAX_ROWS rows; its scratch is a static device array)."""
+    lib = load_library()
+    rc = lib.ns_sample_noalloc(ctypes.byref(args), ctypes.c_void_p(stream))
     if rc != NS_OK:
         raise NsError(rc, lib.ns_last_error().decode(errors="replace"))

@@ -563,6 +563,7 @@ __device__ __forceinline__ void fetch_row_inputs(const NsSampleArgs& a, RowIn& d
 // histograms add up exactly to the one the row kernel would have built.
 constexpr int kPreRows = 256;  // calls with at most this many rows use the pre-pass
 constexpr int kPreParts = 4;   // blocks per row
+static_assert(kPreRows == kRowsScratchRows, "the header's limit is the scratch size");
 
 struct PreStats {
   double z;        // sum over the part of e = exp(s - m0)
@@ -571,10 +572,13 @@ struct PreStats {
   uint32_t pad[2];
 };
 
-// Scratch of the pre-pass (device globals, no allocation): slot r belongs to
-// row r of the current call.  Calls that overlap on the GPU race on it.
-__device__ uint32_t g_pre_hist[kPreRows][kPreParts][kBins];
-__device__ PreStats g_pre_stats[kPreRows][kPreParts];
+// Scratch of the pre-pass: file-scope device arrays of the library (16 MB
+// of histograms and 32 KB of statistics, held by every GPU that loads it);
+// slot r belongs to row r of the current call.  Nothing in them needs
+// clearing: a call reads only slots it wrote earlier in the same call.
+// Calls that overlap on the GPU race on them.
+static __device__ __align__(256) uint32_t g_pre_hist[kPreRows][kPreParts][kBins];
+static __device__ __align__(256) PreStats g_pre_stats[kPreRows][kPreParts];
 
 // Rows the pre-pass serves: top-p on, top-k off, no debug outputs.
 __device__ __forceinline__ bool pre_row(const NsRowParams& P, int V, bool debug) {
@@ -1618,7 +1622,8 @@ __device__ __noinline__ int topk_insert(unsigned long long* wl, int wcnt, const 
 
 // ---------------------------------------------------------------- pre-pass kernel
 template <class E>
-__global__ void __launch_bounds__(kThreads) pre_kernel(const NsSampleArgs a, int W) {
+__device__ __forceinline__ void pre_pass(const NsSampleArgs& a, int W, uint32_t* scratch_hist,
+                                         PreStats* scratch_stats) {
   constexpr int EPT = E::kEPT;
   constexpr int esz = sizeof(typename E::Raw) / EPT;
   __shared__ __align__(16) uint32_t hist[kBins];
@@ -1723,7 +1728,7 @@ __global__ void __launch_bounds__(kThreads) pre_kernel(const NsSampleArgs a, int
     }
   }
   __syncthreads();
-  uint32_t* gh = g_pre_hist[row][part];
+  uint32_t* gh = scratch_hist + ((size_t)row * kPreParts + part) * kBins;
   for (int b = tid; b < kBins / 4; b += kThreads)
     reinterpret_cast<uint4*>(gh)[b] = reinterpret_cast<const uint4*>(hist)[b];
   if (tid == 0) {
@@ -1738,8 +1743,22 @@ __global__ void __launch_bounds__(kThreads) pre_kernel(const NsSampleArgs a, int
     st.mxkey = k;
     st.m0 = m0;
     st.pad[0] = st.pad[1] = 0u;
-    g_pre_stats[row][part] = st;
+    scratch_stats[(size_t)row * kPreParts + part] = st;
   }
+}
+
+// The pre-pass as ns_sample launches it: the scratch named directly.
+template <class E>
+__global__ void __launch_bounds__(kThreads) pre_kernel(const NsSampleArgs a, int W) {
+  pre_pass<E>(a, W, &g_pre_hist[0][0][0], &g_pre_stats[0][0]);
+}
+
+// The same pre-pass given the scratch's device address, which the host
+// looked up with cudaGetSymbolAddress (ns_sample_noalloc).
+template <class E>
+__global__ void __launch_bounds__(kThreads) pre_kernel_at(const NsSampleArgs a, int W, uint32_t* scratch_hist,
+                                                          PreStats* scratch_stats) {
+  pre_pass<E>(a, W, scratch_hist, scratch_stats);
 }
 
 // ---------------------------------------------------------------- one row
@@ -2511,6 +2530,15 @@ struct DevState {
   int blocks_per_sm[2] = {0, 0};
   size_t occ_for[2] = {0, 0};
   int sms = 0;
+  uint32_t* scratch_hist = nullptr;  // device addresses of the pre-pass scratch (ns_sample_noalloc)
+  PreStats* scratch_stats = nullptr;
+};
+
+// Where a launch's pre-pass writes: nullptr in both = the scratch named in
+// device code (ns_sample); else its device address (ns_sample_noalloc).
+struct ScratchAt {
+  uint32_t* hist = nullptr;
+  PreStats* stats = nullptr;
 };
 std::mutex g_mu;
 DevState g_dev[64];
@@ -2524,7 +2552,54 @@ bool rows_supported(const NsSampleArgs& a) {
          ((int64_t)a.logits_row_stride * esize) % 16 == 0 && ((int64_t)a.vocab_size * esize) % 16 == 0;
 }
 
+static int rows_launch_at(const NsSampleArgs& a, cudaStream_t stream, int device, std::string& err,
+                          const rk::ScratchAt& at);
+
 int rows_launch(const NsSampleArgs& a, cudaStream_t stream, int device, std::string& err) {
+  return rows_launch_at(a, stream, device, err, rk::ScratchAt{});
+}
+
+int rows_noalloc_setup(int device, std::string& err) {
+  using namespace rk;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (device < 0 || device >= 64) {
+    err = "device ordinal >= 64";
+    return NS_ERR_UNSUPPORTED;
+  }
+  DevState& ds = g_dev[device];
+  if (ds.scratch_hist && ds.scratch_stats) return NS_OK;
+  // the arrays' names are host-side stand-ins; the kernels need their device
+  // addresses on this (the current) device
+  void* h = nullptr;
+  void* st = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&h, g_pre_hist);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress(&st, g_pre_stats);
+  if (e != cudaSuccess || !h || !st) {
+    err = std::string("cudaGetSymbolAddress of the pre-pass scratch: ") + cudaGetErrorString(e);
+    return NS_ERR_CUDA;
+  }
+  ds.scratch_hist = static_cast<uint32_t*>(h);
+  ds.scratch_stats = static_cast<PreStats*>(st);
+  return NS_OK;
+}
+
+int rows_launch_noalloc(const NsSampleArgs& a, cudaStream_t stream, int device, std::string& err) {
+  using namespace rk;
+  ScratchAt at;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (device < 0 || device >= 64 || !g_dev[device].scratch_hist) {
+      err = "ns_sample_noalloc: the device's scratch address was not set up";
+      return NS_ERR_CUDA;
+    }
+    at.hist = g_dev[device].scratch_hist;
+    at.stats = g_dev[device].scratch_stats;
+  }
+  return rows_launch_at(a, stream, device, err, at);
+}
+
+static int rows_launch_at(const NsSampleArgs& a, cudaStream_t stream, int device, std::string& err,
+                          const rk::ScratchAt& at) {
   using namespace rk;
   const bool bf16 = a.logits_dtype == NS_DTYPE_BF16;
   const int ept = bf16 ? EBF16::kEPT : EF32::kEPT;
@@ -2581,11 +2656,20 @@ int rows_launch(const NsSampleArgs& a, cudaStream_t stream, int device, std::str
   const char* pe_env = std::getenv("NS_PREPASS");  // "0": every row streams in its own block
   int pre_on = (!debug && a.num_rows <= kPreRows && !(pe_env && pe_env[0] == '0')) ? 1 : 0;
   if (pre_on) {
-    const void* pfn = bf16 ? reinterpret_cast<const void*>(&pre_kernel<EBF16>)
-                           : reinterpret_cast<const void*>(&pre_kernel<EF32>);
-    void* pargs[] = {const_cast<NsSampleArgs*>(&a), const_cast<int*>(&W)};
-    const cudaError_t pe =
-        cudaLaunchKernel(pfn, dim3((unsigned)(a.num_rows * kPreParts)), dim3(kThreads), pargs, 0, stream);
+    cudaError_t pe;
+    if (at.hist) {
+      const void* pfn = bf16 ? reinterpret_cast<const void*>(&pre_kernel_at<EBF16>)
+                             : reinterpret_cast<const void*>(&pre_kernel_at<EF32>);
+      uint32_t* h = at.hist;
+      PreStats* st = at.stats;
+      void* pargs[] = {const_cast<NsSampleArgs*>(&a), const_cast<int*>(&W), &h, &st};
+      pe = cudaLaunchKernel(pfn, dim3((unsigned)(a.num_rows * kPreParts)), dim3(kThreads), pargs, 0, stream);
+    } else {
+      const void* pfn = bf16 ? reinterpret_cast<const void*>(&pre_kernel<EBF16>)
+                             : reinterpret_cast<const void*>(&pre_kernel<EF32>);
+      void* pargs[] = {const_cast<NsSampleArgs*>(&a), const_cast<int*>(&W)};
+      pe = cudaLaunchKernel(pfn, dim3((unsigned)(a.num_rows * kPreParts)), dim3(kThreads), pargs, 0, stream);
+    }
     if (pe != cudaSuccess) {
       err = std::string("pre-pass launch: ") + cudaGetErrorString(pe);
       return NS_ERR_CUDA;

@@ -1840,6 +1840,8 @@ struct DeviceState {
 std::mutex g_mu;
 DeviceState g_dev[64];
 
+static_assert(NS_NOALLOC_MAX_ROWS == kRowsScratchRows, "ns_sample_noalloc's limit is the scratch size");
+
 // Batches of at least this many rows use the one-block-per-row kernel.
 constexpr int kRowsMinBatch = 32;
 
@@ -1869,8 +1871,13 @@ int32_t ns_max_vocab(int32_t logits_dtype) {
   return ns::kMaxSlice * ns::kCluster;
 }
 
-int ns_sample(const NsSampleArgs* args, void* stream) {
-  using namespace ns;
+}  // extern "C"
+
+namespace ns {
+
+// One sampling step (ns_sample's body).  `noalloc`: the row kernels' pre-pass
+// is given the device address of its static scratch (ns_sample_noalloc).
+static int sample_call(const NsSampleArgs* args, void* stream, bool noalloc) {
   if (!args) return fail(NS_ERR_INVALID_ARG, "ns_sample: args is NULL");
   const NsSampleArgs& a = *args;
   if (a.num_rows < 0) return fail(NS_ERR_INVALID_ARG, "ns_sample: num_rows < 0");
@@ -1910,7 +1917,7 @@ int ns_sample(const NsSampleArgs* args, void* stream) {
   const SamplePath path = sample_path();
   if (rows_supported(a) && (path == SamplePath::kRows || (path == SamplePath::kAuto && a.num_rows >= kRowsMinBatch))) {
     std::string msg;
-    const int rc = rows_launch(a, st, dev, msg);
+    const int rc = noalloc ? rows_launch_noalloc(a, st, dev, msg) : rows_launch(a, st, dev, msg);
     return rc == NS_OK ? NS_OK : fail(rc, msg);
   }
   const int W = slice_width(a.vocab_size);
@@ -1959,6 +1966,28 @@ int ns_sample(const NsSampleArgs* args, void* stream) {
   err = cudaLaunchKernelEx(&cfg, sample_kernel, a, W, tma_ok, vec16_ok);
   if (err != cudaSuccess) return fail(NS_ERR_CUDA, std::string("sample kernel launch: ") + cudaGetErrorString(err));
   return NS_OK;
+}
+
+}  // namespace ns
+
+extern "C" {
+
+int ns_sample(const NsSampleArgs* args, void* stream) { return ns::sample_call(args, stream, false); }
+
+int ns_sample_noalloc(const NsSampleArgs* args, void* stream) {
+  using namespace ns;
+  if (!args) return fail(NS_ERR_INVALID_ARG, "ns_sample_noalloc: args is NULL");
+  if (args->num_rows > NS_NOALLOC_MAX_ROWS)
+    return fail(NS_ERR_UNSUPPORTED, "ns_sample_noalloc: num_rows " + std::to_string(args->num_rows) +
+                                        " exceeds NS_NOALLOC_MAX_ROWS (" + std::to_string(NS_NOALLOC_MAX_ROWS) +
+                                        "), the rows its static scratch holds; use ns_sample for larger batches");
+  int dev = 0;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(NS_ERR_CUDA, std::string("ns_sample_noalloc: cudaGetDevice: ") + cudaGetErrorString(e));
+  std::string msg;
+  const int rc = rows_noalloc_setup(dev, msg);  // once per device (the current one)
+  if (rc != NS_OK) return fail(rc, "ns_sample_noalloc: " + msg);
+  return sample_call(args, stream, true);
 }
 
 }  // extern "C"

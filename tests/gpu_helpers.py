@@ -34,7 +34,7 @@ def to_bf16_tensor(x: np.ndarray, device) -> torch.Tensor:
 def run_cabi(logits: torch.Tensor, params, histories, uniforms: Optional[np.ndarray] = None,
              sample_indices: Optional[np.ndarray] = None, debug: bool = True, out_i32: bool = False,
              seed: int = 1234, offset: int = 0, row_offset: int = 0,
-             row_order: Optional[torch.Tensor] = None):
+             row_order: Optional[torch.Tensor] = None, entry: str = "ns_sample"):
     """One ns_sample call through ctypes; returns numpy outputs."""
     dev = logits.device
     V = logits.shape[1]
@@ -72,7 +72,7 @@ def run_cabi(logits: torch.Tensor, params, histories, uniforms: Optional[np.ndar
     a.out_probs = probs.data_ptr() if debug else None
     a.status = status.data_ptr()
     a.row_order = row_order.data_ptr() if row_order is not None else None
-    cabi.ns_sample(a, torch.cuda.current_stream(dev).cuda_stream)
+    getattr(cabi, entry)(a, torch.cuda.current_stream(dev).cuda_stream)
     torch.cuda.synchronize(dev)
     res = dict(tokens=out.cpu().numpy().astype(np.int64), status=int(status.item()))
     if debug:
