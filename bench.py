@@ -65,6 +65,12 @@ def parse_args():
     return ap.parse_args()
 
 
+def trace(rank: int, what: str) -> None:
+    """Stage marks on stderr when NS_BENCH_TRACE=1 (for locating a stuck rank)."""
+    if os.environ.get("NS_BENCH_TRACE") == "1":
+        print(f"[rank {rank}] {what}", file=sys.stderr, flush=True)
+
+
 def dist_env():
     return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
 
@@ -246,9 +252,11 @@ def run_ours(args):
             dist.all_gather_into_tensor(gathered, out)
 
     K, Wm = args.steps, max(3, args.warmup)
+    trace(rank, "warm-up")
     for k in range(Wm):
         step(k)
     torch.cuda.synchronize()
+    trace(rank, "capturing")
 
     stream = torch.cuda.Stream()
     graphs = []
@@ -278,6 +286,7 @@ def run_ours(args):
         bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
     except AttributeError:
         bus = str(local)
+    trace(rank, "timing")
     clocks = ClockSampler(bus)
     clocks.start()
     time.sleep(0.1)
@@ -339,6 +348,7 @@ def run_ours(args):
     peak, peak_kind = measured_peaks()
     achieved = algo_bytes / (kern_ms * 1e-3) / 1e9
 
+    trace(rank, "end to end")
     # ---- end to end through the public API from host buffers
     host_logits = logits[0].cpu().pin_memory()
     lg_dev = torch.empty_like(logits[0])
@@ -370,10 +380,20 @@ def run_ours(args):
     del toks
     packed_bytes = packing.layout(pk)[-1]
 
+    # every CUDA graph holding NCCL calls must be gone before the process
+    # group is destroyed, or the teardown waits for them forever
+    trace(rank, "releasing graphs")
+    g_main = g_rem = None
     graphs.clear()
+    torch.cuda.synchronize()
+    import gc
+
+    gc.collect()
     if world > 1:
+        trace(rank, "final barrier")
         dist.barrier()
         dist.destroy_process_group()
+    trace(rank, "done")
     if rank != 0:
         return
     rows_total = ROWS * world
