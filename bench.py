@@ -84,8 +84,8 @@ def measured_peaks():
 
 
 def profiled_traffic():
-    """DRAM bytes per launch of the sampling kernel from the committed ncu summary."""
-    f = REPO / "profiles" / "row_kernel_config2.md"
+    """DRAM bytes of one sampling step (pre-pass + row kernel) from the committed ncu summary."""
+    f = REPO / "profiles" / "pre_and_row_kernels_config2.md"
     if not f.exists():
         return None
     m = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", f.read_text())
