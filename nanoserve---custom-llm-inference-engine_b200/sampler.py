@@ -3,8 +3,10 @@
 ``Sampler(device).sample(logits, sampling_params_list, history_token_ids,
 generators=None)`` keeps the reference signature (sampler.py:17-27) and
 returns int64 token ids on ``logits.device``, so ``engine.py:247-250`` and
-``Scheduler.update_with_sampled`` work unchanged.  The work is one launch of
-the sm_100a kernel behind ``torch.ops.nanoserve_b200.sample``.
+``Scheduler.update_with_sampled`` work unchanged.  The work is one call of
+the sm_100a library behind ``torch.ops.nanoserve_b200.sample``: one kernel
+launch, or two (a top-p pre-pass, then the row kernel) for batches of at most
+256 rows.
 
 Differences from the reference, all additive:
 
