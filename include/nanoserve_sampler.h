@@ -138,8 +138,12 @@ typedef struct NsSampleArgs {
 } NsSampleArgs;
 
 /* Enqueue one sampling step on `stream` (a cudaStream_t; NULL = legacy
- * default stream).  Host-side checks only; no host synchronisation, no
- * allocation.  Replaces sampler.py:21-89 (Sampler.sample). */
+ * default stream): one kernel launch, or two (a top-p pre-pass, then the row
+ * kernel) for calls of at most 256 rows without debug outputs.  Host-side
+ * checks only; no host synchronisation, no allocation.  The pre-pass keeps
+ * its partial results in a static device array of the library, so calls
+ * that overlap on the GPU race on it.  Replaces sampler.py:21-89
+ * (Sampler.sample). */
 int ns_sample(const NsSampleArgs* args, void* stream);
 
 /* Largest num_rows that ns_sample_noalloc accepts. */
