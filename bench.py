@@ -440,7 +440,9 @@ def run_ours(args):
             "d2h_bytes_per_step": rows_total * 4,
             "path": "Sampler.sample(host-pinned logits copied in, Python params/histories packed) + ids .cpu()",
         },
-        "gpu_launches": K,
+        # the library launches the top-p pre-pass before the row kernel when a
+        # call has at most 256 rows and no debug outputs (NS_PREPASS=0: never)
+        "gpu_launches": K * (2 if ROWS <= 256 and os.environ.get("NS_PREPASS") != "0" else 1),
         "clocks": clocks.summary(),
     }
     if cpu is not None:
