@@ -294,3 +294,17 @@ def test_top_p_rows_without_debug_outputs(V, prepass, monkeypatch):
     gpu = H.run_cabi(lg, params, hists, u, debug=False)
     assert gpu["status"] == 0
     _check(H.compare(gpu, np.stack(rows), params, hists, u))
+
+
+@pytest.mark.parametrize("prepass", ["1", "0"])
+def test_config3_bf16_gather_without_debug_outputs(prepass, monkeypatch):
+    """Config 3 as served (64 gathered bf16 rows, top-p 0.95, penalty 1.2, no
+    debug outputs): the bf16 pre-pass and the single-block path both give
+    the oracle's tokens."""
+    monkeypatch.setenv("NS_PREPASS", prepass)
+    dev = _dev()
+    w = W.make(3, seed=34)
+    lg = H.to_bf16_tensor(w.logits, dev)
+    gpu = H.run_cabi(lg, w.params, w.histories, w.uniforms, sample_indices=w.sample_indices, debug=False)
+    assert gpu["status"] == 0
+    _check(H.compare(gpu, w.gathered(), w.params, w.histories, w.uniforms))
