@@ -308,3 +308,59 @@ def test_config3_bf16_gather_without_debug_outputs(prepass, monkeypatch):
     gpu = H.run_cabi(lg, w.params, w.histories, w.uniforms, sample_indices=w.sample_indices, debug=False)
     assert gpu["status"] == 0
     _check(H.compare(gpu, w.gathered(), w.params, w.histories, w.uniforms))
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("V", [32768, 128256])
+def test_top_k_rows_without_debug_outputs(V, dtype):
+    """Top-k rows as served (no debug outputs), mixed with top-p rows that take
+    the pre-pass: ties at the k-th value, k = 1, k = 128 and k = 129 (past the
+    candidate-list path), top-k with top-p, the penalty, NaN / +inf / all -inf
+    rows, a flat row and a mostly -inf row (candidate lists that overflow into
+    the general path) all give the oracle's tokens."""
+    dev = _dev()
+    rng = np.random.default_rng(45)
+    SP = importlib.import_module(H.PKG + ".config").SamplingParams
+    kinds = [
+        ("normal", SP(temperature=1.0, top_k=50)),
+        ("normal", SP(temperature=0.7, top_k=5, repetition_penalty=1.2)),
+        ("normal", SP(temperature=1.0, top_k=1)),
+        ("normal", SP(temperature=1.3, top_k=128, top_p=0.9)),
+        ("normal", SP(temperature=0.9, top_k=20, top_p=0.5, repetition_penalty=0.8)),
+        ("normal", SP(temperature=1.0, top_k=129)),
+        ("flat", SP(temperature=1.0, top_k=40)),
+        ("ties", SP(temperature=1.0, top_k=10)),
+        ("nan", SP(temperature=1.0, top_k=16)),
+        ("pinf", SP(temperature=1.0, top_k=16)),
+        ("ninf", SP(temperature=1.0, top_k=16)),
+        ("normal", SP(temperature=1.0, top_p=0.9)),
+        ("sparse", SP(temperature=1.0, top_k=64)),
+    ]
+    rows, params, hists = [], [], []
+    for r in range(52):
+        kind, p = kinds[r % len(kinds)]
+        x = (rng.standard_normal(V) * 2.0).astype(np.float32)
+        x[rng.integers(0, V, 20)] += 8.0
+        if kind == "flat":
+            x[:] = 0.25
+        elif kind == "ties":
+            x[rng.choice(V, 30, replace=False)] = 20.0
+        elif kind == "nan":
+            x[rng.integers(0, V)] = np.nan
+        elif kind == "pinf":
+            x[rng.integers(0, V)] = np.inf
+        elif kind == "ninf":
+            x[:] = -np.inf
+        elif kind == "sparse":
+            x[rng.random(V) < 0.9] = -np.inf
+        rows.append(x)
+        params.append(p)
+        hists.append(rng.integers(0, V, 700).tolist() if p.repetition_penalty != 1.0 else [])
+    lg = torch.from_numpy(np.stack(rows)).to(dev)
+    if dtype == "bf16":
+        lg = lg.to(torch.bfloat16)
+    ref = lg.float().cpu().numpy()
+    u = rng.random(len(rows)).astype(np.float32)
+    gpu = H.run_cabi(lg, params, hists, u, debug=False)
+    assert gpu["status"] == 0
+    _check(H.compare(gpu, ref, params, hists, u))
