@@ -71,6 +71,8 @@ extern "C" {
                                            kept them in index order       */
 #define NS_STATUS_BAD_ROW_ORDER 0x10u   /* row_order[t] outside [0, S): that
                                            slot took row t instead        */
+#define NS_STATUS_BAD_POOL_RANGE 0x20u  /* ns_history_gather / _append: a
+                                           range or slot outside the pool */
 
 /* One row's sampling parameters (32 bytes, device array [num_rows]).
  * Mirrors nanoserve/config.py:68-79 SamplingParams (temperature :72,
@@ -164,6 +166,31 @@ int ns_sample(const NsSampleArgs* args, void* stream);
  * same outputs as ns_sample.  No counterpart in the reference
  * (nanoserve/scheduler/sampler.py allocates through torch). */
 int ns_sample_noalloc(const NsSampleArgs* args, void* stream);
+
+/* Device-resident histories.  The reference rebuilds each request's prior
+ * token ids as a Python list every step (nanoserve/engine.py:242-246, prompt
+ * + output) and the sampler indexes with them (sampler.py:34).  These two
+ * calls keep the ids in one append-only int32 device pool instead (a region
+ * per request, laid out by the caller) and build a step's CSR histories
+ * (NsSampleArgs.history_offsets / history_ids) on the device.  No
+ * counterpart in the reference.  Both only enqueue one small kernel on
+ * `stream`: no host synchronisation, no allocation.  `status` (device [1] or
+ * NULL) gets NS_STATUS_BAD_POOL_RANGE OR-ed in for ranges outside the pool.
+ *
+ * ns_history_gather: for r < num_rows, out_ids[offsets[r] + j] =
+ *   pool[row_src[r] + j] for j < offsets[r+1] - offsets[r].  A row whose
+ *   source range leaves [0, pool_size) gets ids of -1 instead (ns_sample
+ *   then reports NS_STATUS_BAD_HISTORY_ID).  row_src, offsets: device int64
+ *   [num_rows] and [num_rows + 1]; out_ids: device int32 [offsets[num_rows]].
+ * ns_history_append: pool[row_dst[r]] = tokens[r] for r < num_rows with
+ *   row_dst[r] >= 0 (negative: skip the row).  tokens: device [num_rows],
+ *   int64 or int32 as tokens_dtype (NS_OUT_I64 / NS_OUT_I32) says -- the
+ *   out_tokens of an ns_sample call.  Destinations at or past pool_size are
+ *   not written. */
+int ns_history_gather(const int32_t* pool, int64_t pool_size, const int64_t* row_src, const int64_t* offsets,
+                      int32_t num_rows, int32_t* out_ids, uint32_t* status, void* stream);
+int ns_history_append(int32_t* pool, int64_t pool_size, const int64_t* row_dst, const void* tokens,
+                      int32_t tokens_dtype, int32_t num_rows, uint32_t* status, void* stream);
 
 /* Message for the last non-OK status returned on this host thread. */
 const char* ns_last_error(void);

@@ -7,6 +7,8 @@ Public surface:
   ``torch.ops.nanoserve_b200.sample``;
 * :class:`SamplingParams` -- same fields as nanoserve/config.py:68-79;
 * :mod:`._cabi` -- ctypes binding of ``include/nanoserve_sampler.h``;
+* :class:`HistoryStore` -- device-resident, append-only prior-token
+  histories (replaces the per-step lists of nanoserve/engine.py:242-246);
 * :mod:`.sharded` -- row-sharded sampling over several GPUs (one process per
   GPU, one NCCL all-gather of the sampled ids);
 * :mod:`.workloads` -- seeded synthetic inputs shaped like the benchmark
@@ -14,5 +16,6 @@ Public surface:
 """
 from .config import SamplingParams
 from .sampler import Sampler, load_ops
+from .history import HistoryStore
 
-__all__ = ["Sampler", "SamplingParams", "load_ops"]
+__all__ = ["HistoryStore", "Sampler", "SamplingParams", "load_ops"]

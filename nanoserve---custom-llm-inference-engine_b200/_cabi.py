@@ -34,9 +34,11 @@ NS_STATUS_BAD_HISTORY_ID = 0x2
 NS_STATUS_WAIT_TIMEOUT = 0x4
 NS_STATUS_CAP_OVERFLOW = 0x8
 NS_STATUS_BAD_ROW_ORDER = 0x10
+NS_STATUS_BAD_POOL_RANGE = 0x20
 
 # every entry point the header declares
-EXPORTED_SYMBOLS = ("ns_sample", "ns_sample_noalloc", "ns_last_error", "ns_abi_version", "ns_max_vocab")
+EXPORTED_SYMBOLS = ("ns_sample", "ns_sample_noalloc", "ns_history_gather", "ns_history_append", "ns_last_error",
+                    "ns_abi_version", "ns_max_vocab")
 NS_NOALLOC_MAX_ROWS = 256
 
 
@@ -101,6 +103,12 @@ def load_library() -> ctypes.CDLL:
         lib.ns_sample.restype = ctypes.c_int
         lib.ns_sample_noalloc.argtypes = [ctypes.POINTER(NsSampleArgs), ctypes.c_void_p]
         lib.ns_sample_noalloc.restype = ctypes.c_int
+        lib.ns_history_gather.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+                                          ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        lib.ns_history_gather.restype = ctypes.c_int
+        lib.ns_history_append.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+                                          ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]
+        lib.ns_history_append.restype = ctypes.c_int
         lib.ns_last_error.argtypes = []
         lib.ns_last_error.restype = ctypes.c_char_p
         lib.ns_abi_version.argtypes = []
@@ -129,5 +137,25 @@ def ns_sample_noalloc(args: NsSampleArgs, stream: int = 0) -> None:
     NS_NOALLOC_MAX_ROWS rows; its scratch is a static device array)."""
     lib = load_library()
     rc = lib.ns_sample_noalloc(ctypes.byref(args), ctypes.c_void_p(stream))
+    if rc != NS_OK:
+        raise NsError(rc, lib.ns_last_error().decode(errors="replace"))
+
+
+def ns_history_gather(pool: int, pool_size: int, row_src: int, offsets: int, num_rows: int, out_ids: int,
+                      status: int = 0, stream: int = 0) -> None:
+    """Build one step's CSR history ids from a device pool (device pointers as ints)."""
+    lib = load_library()
+    rc = lib.ns_history_gather(pool or None, pool_size, row_src or None, offsets or None, num_rows,
+                               out_ids or None, status or None, ctypes.c_void_p(stream))
+    if rc != NS_OK:
+        raise NsError(rc, lib.ns_last_error().decode(errors="replace"))
+
+
+def ns_history_append(pool: int, pool_size: int, row_dst: int, tokens: int, tokens_dtype: int, num_rows: int,
+                      status: int = 0, stream: int = 0) -> None:
+    """Append one sampled id per row to the device pool (device pointers as ints)."""
+    lib = load_library()
+    rc = lib.ns_history_append(pool or None, pool_size, row_dst or None, tokens or None, tokens_dtype, num_rows,
+                               status or None, ctypes.c_void_p(stream))
     if rc != NS_OK:
         raise NsError(rc, lib.ns_last_error().decode(errors="replace"))
