@@ -78,13 +78,9 @@ def plan_step(params: Sequence, starts: np.ndarray, lengths: np.ndarray, vocab: 
     ``packing.pack``, only rows with the penalty on carry ids (the others get
     an empty range).  Returns (rows, offsets int64 [S+1], src int64 [S])."""
     S = len(params)
-    rows = np.empty(S, dtype=packing.ROW_DTYPE)
-    lens = np.zeros(S, dtype=np.int64)
-    for i, p in enumerate(params):
-        rec = packing.derive_row(p, vocab, int(lengths[i]))
-        rows[i] = rec
-        if rec[4] & _cabi.NS_ROW_PENALTY:
-            lens[i] = lengths[i]
+    lengths = np.asarray(lengths, dtype=np.int64)
+    rows = packing.derive_rows(params, vocab, lengths)
+    lens = np.where((rows["flags"] & _cabi.NS_ROW_PENALTY) != 0, lengths, 0)
     offsets = np.zeros(S + 1, dtype=np.int64)
     np.cumsum(lens, out=offsets[1:])
     src = np.asarray(starts, dtype=np.int64).copy()

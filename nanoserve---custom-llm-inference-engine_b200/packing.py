@@ -64,6 +64,33 @@ def derive_row(p, vocab: int, hist_len: int) -> tuple:
     return (np.float32(temp), top_p32, np.float32(rp), k_eff, flags, 0, seed_u64)
 
 
+def derive_rows(params: Sequence, vocab: int, hist_lens) -> np.ndarray:
+    """``derive_row`` for every row at once (ROW_DTYPE [S]), bit for bit the
+    same records: the comparisons run on float64 arrays, as Python compares
+    floats, and each value is rounded to float32 once."""
+    S = len(params)
+    rows = np.zeros(S, dtype=ROW_DTYPE)
+    if S == 0:
+        return rows
+    t = np.array([p.temperature for p in params], dtype=np.float64)
+    tp = np.array([p.top_p for p in params], dtype=np.float64)
+    rp = np.array([p.repetition_penalty for p in params], dtype=np.float64)
+    lens = np.asarray(hist_lens, dtype=np.int64)
+    with np.errstate(invalid="ignore"):
+        rows["temperature"] = np.where(t > 0, np.maximum(t, 1e-6), 1.0).astype(np.float32)
+        rows["top_p"] = np.where(tp < 1.0, tp, 1.0).astype(np.float32)
+        rows["repetition_penalty"] = rp.astype(np.float32)
+        flags = np.where(t == 0.0, _cabi.NS_ROW_GREEDY, 0) | np.where(tp < 1.0, _cabi.NS_ROW_TOP_P, 0)
+        flags |= np.where((rp != 1.0) & (lens > 0), _cabi.NS_ROW_PENALTY, 0)
+    rows["top_k"] = [int(k) if (k > 0 and k < vocab) else 0 for k in (p.top_k for p in params)]
+    seeds = [getattr(p, "seed", None) for p in params]
+    if any(sd is not None for sd in seeds):
+        flags |= np.array([_cabi.NS_ROW_SEED if sd is not None else 0 for sd in seeds])
+        rows["seed"] = [int(sd) & 0xFFFFFFFFFFFFFFFF if sd is not None else 0 for sd in seeds]
+    rows["flags"] = flags
+    return rows
+
+
 # Relative cost of a row on the one-block-per-row kernel, by the path it
 # takes there (greedy; top-k <= 128 with or without top-p; top-p alone, large
 # top-k or plain sampling), from measured single-row times on B200.
@@ -134,16 +161,11 @@ def pack(params: Sequence, histories: Sequence[Sequence[int]], vocab: int, sms: 
     S = len(params)
     if len(histories) < S:
         raise IndexError("history_token_ids has fewer entries than sampling_params_list")
-    rows = np.empty(S, dtype=ROW_DTYPE)
-    active = []
-    lens = np.zeros(S, dtype=np.int64)
-    for i, p in enumerate(params):
-        h = histories[i]
-        rec = derive_row(p, vocab, len(h))
-        rows[i] = rec
-        if rec[4] & _cabi.NS_ROW_PENALTY:
-            active.append(h)
-            lens[i] = len(h)
+    hl = np.fromiter((len(histories[i]) for i in range(S)), dtype=np.int64, count=S)
+    rows = derive_rows(params, vocab, hl)
+    pen = (rows["flags"] & _cabi.NS_ROW_PENALTY) != 0
+    lens = np.where(pen, hl, 0)
+    active = [histories[i] for i in np.flatnonzero(pen)]
     offsets = np.zeros(S + 1, dtype=np.int64)
     np.cumsum(lens, out=offsets[1:])
     total = int(offsets[-1])

@@ -119,3 +119,32 @@ def test_order_travels_in_the_staging_buffer():
     buf = packing.to_bytes(pk)
     a, b, c, d, end = packing.layout(pk)
     assert d % 16 == 0 and np.array_equal(buf[d : d + 4 * 300].view(np.int32), pk.order)
+
+
+def test_derive_rows_equals_derive_row_on_edge_values():
+    """The vectorised row packing gives derive_row's records bit for bit,
+    across the comparisons' edge values (zero, negative and NaN temperatures,
+    top_p at and past 1, NaN top_p and penalty, top_k at the vocabulary size,
+    seeds beyond 64 bits)."""
+    import itertools
+    import numpy as np
+    from conftest import pkg
+
+    packing = pkg("packing")
+    SP = pkg("config").SamplingParams
+    V = 1000
+    temps = [0.0, -0.0, -1.0, 1e-9, 1e-6, 0.7, 1.0, 2.5, float("nan"), float("inf")]
+    tps = [1.0, 0.9, 0.0, 1.5, float("nan"), 0.999999999]
+    tks = [-1, 0, 1, 50, V - 1, V, V + 5]
+    rps = [1.0, 1.1, 0.8, float("nan"), 0.0]
+    lens = [0, 3]
+    params, hl = [], []
+    for i, (t, tp, k, rp, n) in enumerate(itertools.product(temps, tps, tks, rps, lens)):
+        p = SP(temperature=t, top_p=tp, top_k=k, repetition_penalty=rp)
+        if i % 7 == 0:
+            p.seed = [5, -1, 2**70 + 3][i % 3]
+        params.append(p)
+        hl.append(n)
+    got = packing.derive_rows(params, V, hl)
+    want = np.array([packing.derive_row(p, V, n) for p, n in zip(params, hl)], dtype=packing.ROW_DTYPE)
+    assert got.tobytes() == want.tobytes()
