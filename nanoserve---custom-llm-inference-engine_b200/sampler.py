@@ -19,7 +19,10 @@ Differences from the reference, all additive:
   ``(seed, step, row)`` instead of the global generator that
   ``torch.multinomial`` uses (sampler.py:87); ``SamplingParams.seed``, which
   the reference ignores, gives a row its own key;
-* ``generators`` is accepted and ignored, as in the reference (sampler.py:26).
+* ``generators`` is accepted and ignored, as in the reference (sampler.py:26);
+* ``sample_async`` returns int32 ids through a non-blocking copy to pinned
+  host memory (``PendingTokens.wait()``), in place of the caller's blocking
+  ``.tolist()`` (engine.py:250).
 
 There is no CPU path: the op raises if the CUDA library is not built or the
 tensors are not on a CUDA device.
@@ -69,6 +72,56 @@ class _Staging:
         return self.host[:nbytes]
 
 
+class PendingTokens:
+    """Sampled ids on their way to the host: an int32 copy into pinned memory,
+    enqueued behind the sampling kernel, and the event that marks its end.
+    ``wait()`` blocks until then and returns the ids as a list (what
+    ``engine.py:250`` gets from ``.tolist()``)."""
+
+    def __init__(self, host: torch.Tensor, event: torch.cuda.Event, n: int):
+        self._host = host
+        self._event = event
+        self._n = n
+        self._ids: Optional[List[int]] = None
+
+    def ready(self) -> bool:
+        return self._ids is not None or self._event.query()
+
+    def wait(self) -> List[int]:
+        if self._ids is None:
+            self._event.synchronize()
+            self._ids = self._host[: self._n].numpy().tolist()
+        return self._ids
+
+
+class _HostRing:
+    """A few pinned int32 buffers reused round robin for PendingTokens; a
+    buffer is handed out again only after its previous copy has finished."""
+
+    def __init__(self, slots: int = 4):
+        self._bufs: List[Optional[torch.Tensor]] = [None] * slots
+        self._pending: List[Optional[PendingTokens]] = [None] * slots
+        self._next = 0
+
+    def copy(self, tokens: torch.Tensor) -> PendingTokens:
+        i = self._next
+        self._next = (i + 1) % len(self._bufs)
+        prev = self._pending[i]
+        if prev is not None:
+            prev.wait()  # its list is taken before the buffer is reused
+        n = tokens.numel()
+        if self._bufs[i] is None or self._bufs[i].numel() < n:
+            self._bufs[i] = torch.empty(max(n, 1024), dtype=torch.int32, pin_memory=True)
+        host = self._bufs[i]
+        src = tokens if tokens.dtype == torch.int32 else tokens.to(torch.int32)
+        host[:n].copy_(src, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        pt = PendingTokens(host, ev, n)
+        self._pending[i] = pt
+        return pt
+
+
 class Sampler:
     """B200 sampling op with the reference ``Sampler`` interface."""
 
@@ -76,7 +129,26 @@ class Sampler:
         self.device = torch.device(device)
         self._step = 0
         self._staging = _Staging()
+        self._ring = _HostRing()
         load_ops()
+
+    def sample_async(self, logits: torch.Tensor, sampling_params_list: List,
+                     history_token_ids: List[List[int]], generators=None, **kw) -> PendingTokens:
+        """``sample`` with int32 ids and a non-blocking copy to pinned host
+        memory in place of the caller's blocking ``.tolist()`` (engine.py:250):
+        the host can prepare the next step while this one samples, then
+        ``wait()``.  Up to four results may be outstanding at once; a fifth
+        call first waits for the oldest."""
+        if kw.get("return_debug"):
+            raise ValueError("sample_async returns ids only; use sample(return_debug=True) for debug outputs")
+        kw["out_dtype"] = torch.int32
+        out = self.sample(logits, sampling_params_list, history_token_ids, generators, **kw)
+        return self._ring.copy(out)
+
+    def to_host_async(self, tokens: torch.Tensor) -> PendingTokens:
+        """Non-blocking int32 copy of device ids (e.g. from ``sample_packed`` or
+        ``HistoryStore.sample``) to pinned host memory."""
+        return self._ring.copy(tokens)
 
     # -- the reference entry point (sampler.py:21-27) ---------------------
     def sample(
