@@ -11,9 +11,10 @@
  * top-p sampler.py:60-73, softmax + NaN guard sampler.py:75-80, greedy
  * argmax sampler.py:82-83, multinomial sampler.py:84-89).  Here the whole
  * chain is one kernel launch per call with one HBM pass per vocabulary row:
- * batches of 32 or more aligned rows take one thread block per row that
- * streams the row through shared memory; smaller batches take an 8-CTA
- * thread-block cluster per row that holds it in distributed shared memory.
+ * batches of 32 or more aligned rows take the row kernel (one block per SM
+ * streams whole rows through a bulk-copy ring and finishes each row while
+ * the next one streams); smaller batches take an 8-CTA thread-block cluster
+ * per row that holds it in distributed shared memory.
  *
  * Everything in this header is plain C: raw pointers, sizes and a stream
  * handle.  All pointers named "device" must be CUDA device (or managed)
@@ -38,7 +39,7 @@
 extern "C" {
 #endif
 
-#define NS_ABI_VERSION 2
+#define NS_ABI_VERSION 3
 
 /* status codes returned by every entry point */
 #define NS_OK 0
@@ -53,6 +54,14 @@ extern "C" {
 /* output token types */
 #define NS_OUT_I64 0
 #define NS_OUT_I32 1
+
+/* NsSampleArgs.kernel: which kernel serves the call */
+#define NS_KERNEL_AUTO 0     /* split-row for batches of >= 32 aligned rows,
+                                the cluster kernel otherwise              */
+#define NS_KERNEL_CLUSTER 1  /* always the cluster kernel                 */
+#define NS_KERNEL_SPLIT 2    /* the split-row kernel where its layout
+                                conditions hold (aligned rows, vocabulary
+                                in [24576, 196608]), else the cluster one */
 
 /* NsRowParams.flags bits */
 #define NS_ROW_GREEDY 0x1u   /* temperature == 0.0: argmax token          */
@@ -84,7 +93,8 @@ typedef struct NsRowParams {
   float repetition_penalty; /* used when NS_ROW_PENALTY                  */
   int32_t top_k;            /* 0 = off                                   */
   uint32_t flags;           /* NS_ROW_* bits                             */
-  uint32_t reserved;
+  uint32_t seed_step;       /* NS_ROW_SEED: the request's own step index
+                               (e.g. its token count), the Philox counter */
   uint64_t seed;            /* per-row Philox key when NS_ROW_SEED       */
 } NsRowParams;
 
@@ -95,10 +105,12 @@ typedef struct NsRowParams {
  * history_ids[history_offsets[i] .. history_offsets[i+1]).
  *
  * Randomness: when uniforms is non-NULL, row i draws with the caller's
- * uniform uniforms[i] in [0,1); otherwise from Philox4x32-10 with key
- * (philox_seed, or the row's seed under NS_ROW_SEED) and counter
- * (philox_offset, row_offset + i).  The draw is an inverse CDF over the
- * filtered probabilities in vocabulary order.
+ * uniform uniforms[i] in [0,1); otherwise from Philox4x32-10: key
+ * philox_seed and counter (philox_offset, row_offset + i), or, for a row
+ * with NS_ROW_SEED, key row_params[i].seed and counter
+ * (row_params[i].seed_step, 0), so that a seeded request draws the same
+ * stream whatever batch or position it is sampled in.  The draw is an
+ * inverse CDF over the filtered probabilities in vocabulary order.
  *
  * Debug outputs (NULL = not written), all [num_rows, vocab] fp32:
  *   out_penalized : the logits after the repetition penalty, i.e. what the
@@ -133,37 +145,54 @@ typedef struct NsSampleArgs {
                                         which the kernel takes rows, a
                                         permutation of [0, S).  A scheduling
                                         hint only: outputs do not depend on
-                                        it.  Putting the most expensive rows
-                                        (top-p without top-k) where they
-                                        share no SM with each other shortens
-                                        mixed batches. */
+                                        it.  Taking the rows with the
+                                        longest finishing work (top-p
+                                        without top-k) first shortens mixed
+                                        batches. */
+  int32_t kernel;                    /* NS_KERNEL_* (0: automatic choice)   */
+  int32_t reserved;                  /* must be 0                          */
+  void* workspace;                   /* device scratch of workspace_bytes
+                                        bytes (ns_workspace_bytes(): the row
+                                        kernel's row-ticket counter), all
+                                        zero before its first use; every
+                                        call leaves it all zero again.  Calls
+                                        that may overlap on the GPU need
+                                        separate workspaces. */
+  int64_t workspace_bytes;
 } NsSampleArgs;
 
 /* Enqueue one sampling step on `stream` (a cudaStream_t; NULL = legacy
- * default stream): one kernel launch, or two (a top-p pre-pass, then the row
- * kernel) for calls of at most 256 rows without debug outputs.  Host-side
- * checks only; no host synchronisation, no allocation.  The pre-pass keeps
- * its partial results in a static device array of the library, so calls
- * that overlap on the GPU race on it.  Replaces sampler.py:21-89
- * (Sampler.sample). */
+ * default stream): one kernel launch.  Host-side checks only; no host
+ * synchronisation, no allocation.  Calls that take the row kernel hand out
+ * their rows through a counter in args->workspace (required for them:
+ * NS_ERR_INVALID_ARG without one); cluster-kernel calls need none.
+ * Replaces sampler.py:21-89 (Sampler.sample). */
 int ns_sample(const NsSampleArgs* args, void* stream);
 
-/* Largest num_rows that ns_sample_noalloc accepts. */
-#define NS_NOALLOC_MAX_ROWS 256
+/* Bytes of NsSampleArgs.workspace for calls of up to num_rows rows (128:
+ * the same for every call).  No counterpart in the reference. */
+int64_t ns_workspace_bytes(int32_t num_rows);
+
+/* Bytes of ns_sample_noalloc's static workspace. */
+#define NS_NOALLOC_WORKSPACE_BYTES 128
 
 /* ns_sample for callers that must not allocate device memory: an engine that
- * reserves all of the GPU's memory for its own pool at start-up and makes no
- * cudaMalloc afterwards, or a host that embeds this library under a strict
- * memory budget.  It allocates nothing on any call.  Every scratch buffer it
- * needs is a file-scope static device array of the library (16 MB, room for
- * NS_NOALLOC_MAX_ROWS rows), which every GPU that loads the library holds
- * until the process exits.  Calls with more rows return NS_ERR_UNSUPPORTED
- * (ns_sample serves them).  The first call on each device looks up the
- * array's device address once, so make that first call outside any stream
- * capture.  Every call shares the array, ns_sample's calls included; nothing
- * in it needs to start at zero, but calls that overlap on the GPU (different
- * streams, or several host threads at once) race on it.  Same arguments and
- * same outputs as ns_sample.  No counterpart in the reference
+ * hands all of the GPU's memory to its own pool at start-up and makes no
+ * cudaMalloc afterwards, or a host that embeds this library under a fixed
+ * memory budget.  It allocates nothing on any call and ignores
+ * args->workspace: its scratch is a file-scope static device array of the
+ * library (NS_NOALLOC_WORKSPACE_BYTES bytes, the row kernel's row-ticket
+ * counter), zero when the library loads, which every GPU that loads the
+ * library holds until the process exits.  The array's size does not depend
+ * on the call, so it limits no call; calls it cannot serve at all (a
+ * vocabulary beyond ns_max_vocab) fail with NS_ERR_UNSUPPORTED and a
+ * message, as ns_sample's do.  Every call looks up the array's device address
+ * on the current device (cudaGetSymbolAddress, a host-side query); the first
+ * one on a device may load the library's GPU code, so make it outside any
+ * stream capture.  Every call shares the array and leaves it zero, as it
+ * found it; calls that overlap on the GPU (different streams, or several host
+ * threads at once) race on it.  Same arguments (but the workspace) and same
+ * outputs as ns_sample.  No counterpart in the reference
  * (nanoserve/scheduler/sampler.py allocates through torch). */
 int ns_sample_noalloc(const NsSampleArgs* args, void* stream);
 

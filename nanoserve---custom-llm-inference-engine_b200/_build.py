@@ -47,20 +47,33 @@ def _stale(target: Path, sources: list[Path]) -> bool:
 
 
 def build_library(force: bool = False, verbose: bool = False) -> Path:
-    """Compile the kernels + C ABI into ``libnanoserve_sampler.so``."""
+    """Compile the kernels + C ABI into ``libnanoserve_sampler.so``: every
+    ``.cu`` file to an object in parallel (``_build/`` next to this file),
+    then one link with the static CUDA runtime."""
     out = PKG_DIR / LIB_NAME
-    srcs = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [INCLUDE / "nanoserve_sampler.h"]
+    cus = sorted(CSRC.glob("*.cu"))
+    srcs = cus + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [INCLUDE / "nanoserve_sampler.h"]
     if not force and not _stale(out, srcs):
         return out
-    cmd = [
-        _nvcc(), *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17",
-        "-Xcompiler", "-fPIC", "-shared", "-cudart", "static",
-        f"-I{INCLUDE}", *[str(s) for s in sorted(CSRC.glob("*.cu"))],
-        "-o", str(out), "-ldl", "-lrt", "-lpthread",
-    ]
+    objdir = PKG_DIR / "_build"
+    objdir.mkdir(exist_ok=True)
+    flags = [*ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", f"-I{INCLUDE}"]
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-    _run(cmd)
+        flags.append("-Xptxas=-v")
+    procs = []
+    for cu in cus:
+        obj = objdir / (cu.stem + ".o")
+        cmd = [_nvcc(), *flags, "-c", str(cu), "-o", str(obj)]
+        procs.append((cmd, obj, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)))
+    objs = []
+    for cmd, obj, p in procs:
+        so, se = p.communicate()
+        if p.returncode != 0:
+            raise RuntimeError(f"build step failed: {' '.join(cmd)}\n{so}\n{se}")
+        if verbose and se:
+            print(se)
+        objs.append(str(obj))
+    _run([_nvcc(), *ARCH_FLAGS, "-shared", "-cudart", "static", *objs, "-o", str(out), "-ldl", "-lrt", "-lpthread"])
     return out
 
 

@@ -24,6 +24,10 @@ NS_DTYPE_BF16 = 1
 NS_OUT_I64 = 0
 NS_OUT_I32 = 1
 
+NS_KERNEL_AUTO = 0
+NS_KERNEL_CLUSTER = 1
+NS_KERNEL_SPLIT = 2
+
 NS_ROW_GREEDY = 0x1
 NS_ROW_TOP_P = 0x2
 NS_ROW_PENALTY = 0x4
@@ -37,9 +41,10 @@ NS_STATUS_BAD_ROW_ORDER = 0x10
 NS_STATUS_BAD_POOL_RANGE = 0x20
 
 # every entry point the header declares
-EXPORTED_SYMBOLS = ("ns_sample", "ns_sample_noalloc", "ns_history_gather", "ns_history_append", "ns_last_error",
-                    "ns_abi_version", "ns_max_vocab")
-NS_NOALLOC_MAX_ROWS = 256
+EXPORTED_SYMBOLS = ("ns_sample", "ns_sample_noalloc", "ns_workspace_bytes", "ns_history_gather",
+                    "ns_history_append", "ns_last_error", "ns_abi_version", "ns_max_vocab")
+NS_ABI_VERSION = 3
+NS_NOALLOC_WORKSPACE_BYTES = 128
 
 
 class NsRowParams(ctypes.Structure):
@@ -49,7 +54,7 @@ class NsRowParams(ctypes.Structure):
         ("repetition_penalty", ctypes.c_float),
         ("top_k", ctypes.c_int32),
         ("flags", ctypes.c_uint32),
-        ("reserved", ctypes.c_uint32),
+        ("seed_step", ctypes.c_uint32),
         ("seed", ctypes.c_uint64),
     ]
 
@@ -77,6 +82,10 @@ class NsSampleArgs(ctypes.Structure):
         ("out_probs", ctypes.c_void_p),
         ("status", ctypes.c_void_p),
         ("row_order", ctypes.c_void_p),
+        ("kernel", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_int64),
     ]
 
 
@@ -115,6 +124,8 @@ def load_library() -> ctypes.CDLL:
         lib.ns_abi_version.restype = ctypes.c_int
         lib.ns_max_vocab.argtypes = [ctypes.c_int32]
         lib.ns_max_vocab.restype = ctypes.c_int32
+        lib.ns_workspace_bytes.argtypes = [ctypes.c_int32]
+        lib.ns_workspace_bytes.restype = ctypes.c_int64
         _lib = lib
     return _lib
 
@@ -133,12 +144,17 @@ def ns_sample(args: NsSampleArgs, stream: int = 0) -> None:
 
 
 def ns_sample_noalloc(args: NsSampleArgs, stream: int = 0) -> None:
-    """The entry point for callers that cannot allocate device memory (at most
-    NS_NOALLOC_MAX_ROWS rows; its scratch is a static device array)."""
+    """The entry point for callers that cannot allocate device memory: it
+    ignores ``args.workspace`` and runs on the library's static workspace."""
     lib = load_library()
     rc = lib.ns_sample_noalloc(ctypes.byref(args), ctypes.c_void_p(stream))
     if rc != NS_OK:
         raise NsError(rc, lib.ns_last_error().decode(errors="replace"))
+
+
+def ns_workspace_bytes(num_rows: int) -> int:
+    """Bytes of ``NsSampleArgs.workspace`` for calls of up to ``num_rows`` rows."""
+    return int(load_library().ns_workspace_bytes(int(num_rows)))
 
 
 def ns_history_gather(pool: int, pool_size: int, row_src: int, offsets: int, num_rows: int, out_ids: int,

@@ -11,6 +11,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/nanoserve_sampler.h"
+
 namespace ns {
 
 // ----------------------------------------------------------------- smem / DSMEM
@@ -302,6 +304,26 @@ __host__ __device__ __forceinline__ double philox_uniform(uint64_t key, uint64_t
   U4 o = philox4x32_10(c, (uint32_t)key, (uint32_t)(key >> 32));
   uint64_t a = o.x >> 5, b = o.y >> 6;  // 27 + 26 bits
   return (double)((a << 26) | b) * (1.0 / 9007199254740992.0);
+}
+
+// The uniform that drives row `row` of a call, clamped to [0, 1): the
+// caller's uniforms[row] when given; else Philox4x32-10.  A row with
+// NS_ROW_SEED uses its own key (the request's seed) and counter (seed_step,
+// 0), so a seeded request draws the same numbers whatever batch it is in,
+// wherever it sits in it and however many steps the sampler has run; other
+// rows use key philox_seed and counter (philox_offset, row_offset + row).
+__device__ __forceinline__ double row_uniform(const NsSampleArgs& a, const NsRowParams& P, int row) {
+  double u;
+  if (a.uniforms) {
+    u = (double)a.uniforms[row];
+  } else if (P.flags & NS_ROW_SEED) {
+    u = philox_uniform(P.seed, (uint64_t)P.seed_step, 0ull);
+  } else {
+    u = philox_uniform(a.philox_seed, a.philox_offset, (uint64_t)(a.row_offset + row));
+  }
+  if (!(u >= 0.0)) u = 0.0;
+  if (u >= 1.0) u = 0x1.fffffffffffffp-1;
+  return u;
 }
 
 }  // namespace ns

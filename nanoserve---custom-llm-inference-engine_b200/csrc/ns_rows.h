@@ -1,5 +1,5 @@
-// ns_rows.h -- host-side entry points of the one-block-per-row sampling
-// kernel (ns_rows.cu), used by ns_sample() in ns_sample.cu.
+// ns_rows.h -- host-side entry points of the split-row sampling kernel
+// (ns_rows.cu), used by ns_sample() in ns_sample.cu.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -10,22 +10,20 @@
 
 namespace ns {
 
-// True when the row kernel can serve this call: 16-byte aligned rows whose
-// byte length is a multiple of 16 and a vocabulary in the supported range.
+// True when the split-row kernel can serve this call: 16-byte aligned rows
+// whose byte length is a multiple of 16 and a vocabulary in the supported
+// range.
 bool rows_supported(const NsSampleArgs& a);
 
-// Launches the row kernel; returns NS_OK or an NS_ERR_* code with `err` set.
+// Bytes of workspace for calls of up to num_rows rows (ns_workspace_bytes).
+int64_t rows_workspace_bytes(int32_t num_rows);
+
+// Launches the split-row kernel on a.workspace; returns NS_OK or an NS_ERR_*
+// code with `err` set.
 int rows_launch(const NsSampleArgs& a, cudaStream_t stream, int device, std::string& err);
 
-// Rows the row kernels' static scratch holds (ns_sample_noalloc's limit).
-constexpr int kRowsScratchRows = 256;
-
-// Once per device, with that device current: looks up the device address of
-// the static pre-pass scratch (cudaGetSymbolAddress) and keeps it.
-int rows_noalloc_setup(int device, std::string& err);
-
-// rows_launch whose pre-pass is given that address instead of naming the
-// scratch; rows_noalloc_setup must have run on `device`.
+// The same on the library's static workspace (ns_sample_noalloc): its device
+// address is looked up with cudaGetSymbolAddress on the current device.
 int rows_launch_noalloc(const NsSampleArgs& a, cudaStream_t stream, int device, std::string& err);
 
 }  // namespace ns

@@ -1076,15 +1076,7 @@ __device__ __forceinline__ void process_row(const NsSampleArgs& a, const Src& S,
   if (bad_row && leader && tid == 0 && status) atomicOr(status, NS_STATUS_BAD_SAMPLE_INDEX);
 
   // row uniform
-  double u;
-  if (a.uniforms) {
-    u = (double)a.uniforms[row];
-  } else {
-    const uint64_t key = (P.flags & NS_ROW_SEED) ? P.seed : a.philox_seed;
-    u = philox_uniform(key, a.philox_offset, (uint64_t)(a.row_offset + row));
-  }
-  if (!(u >= 0.0)) u = 0.0;
-  if (u >= 1.0) u = 0x1.fffffffffffffp-1;
+  const double u = row_uniform(a, P, row);
 
   wait_chunk(g, ctl, warp, par, status);
 
@@ -1840,18 +1832,8 @@ struct DeviceState {
 std::mutex g_mu;
 DeviceState g_dev[64];
 
-static_assert(NS_NOALLOC_MAX_ROWS == kRowsScratchRows, "ns_sample_noalloc's limit is the scratch size");
-
-// Batches of at least this many rows use the one-block-per-row kernel.
+// Batches of at least this many rows use the split-row kernel.
 constexpr int kRowsMinBatch = 32;
-
-enum class SamplePath { kAuto, kCluster, kRows };
-SamplePath sample_path() {
-  const char* e = std::getenv("NS_SAMPLE_PATH");
-  if (e && std::strcmp(e, "cluster") == 0) return SamplePath::kCluster;
-  if (e && std::strcmp(e, "rows") == 0) return SamplePath::kRows;
-  return SamplePath::kAuto;
-}
 
 int slice_width(int V) {
   const int W = (V + kCluster - 1) / kCluster;
@@ -1871,12 +1853,14 @@ int32_t ns_max_vocab(int32_t logits_dtype) {
   return ns::kMaxSlice * ns::kCluster;
 }
 
+int64_t ns_workspace_bytes(int32_t num_rows) { return ns::rows_workspace_bytes(num_rows); }
+
 }  // extern "C"
 
 namespace ns {
 
-// One sampling step (ns_sample's body).  `noalloc`: the row kernels' pre-pass
-// is given the device address of its static scratch (ns_sample_noalloc).
+// One sampling step (ns_sample's body).  `noalloc`: the split-row kernel runs
+// on the library's static workspace (ns_sample_noalloc).
 static int sample_call(const NsSampleArgs* args, void* stream, bool noalloc) {
   if (!args) return fail(NS_ERR_INVALID_ARG, "ns_sample: args is NULL");
   const NsSampleArgs& a = *args;
@@ -1911,11 +1895,11 @@ static int sample_call(const NsSampleArgs* args, void* stream, bool noalloc) {
   if (err != cudaSuccess) return fail(NS_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(err));
   const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
-  // Kernel choice: one block per row once the batch is large enough, the
-  // cluster kernel otherwise.  NS_SAMPLE_PATH=cluster|rows forces one of them
-  // (rows only where its layout conditions hold).
-  const SamplePath path = sample_path();
-  if (rows_supported(a) && (path == SamplePath::kRows || (path == SamplePath::kAuto && a.num_rows >= kRowsMinBatch))) {
+  if (a.kernel != NS_KERNEL_AUTO && a.kernel != NS_KERNEL_CLUSTER && a.kernel != NS_KERNEL_SPLIT)
+    return fail(NS_ERR_INVALID_ARG, "ns_sample: kernel must be NS_KERNEL_AUTO, NS_KERNEL_CLUSTER or NS_KERNEL_SPLIT");
+  // Kernel choice: the split-row kernel once the batch is large enough, the
+  // cluster kernel otherwise (NsSampleArgs.kernel may force either).
+  if (rows_supported(a) && (a.kernel == NS_KERNEL_SPLIT || (a.kernel == NS_KERNEL_AUTO && a.num_rows >= kRowsMinBatch))) {
     std::string msg;
     const int rc = noalloc ? rows_launch_noalloc(a, st, dev, msg) : rows_launch(a, st, dev, msg);
     return rc == NS_OK ? NS_OK : fail(rc, msg);
@@ -1977,16 +1961,6 @@ int ns_sample(const NsSampleArgs* args, void* stream) { return ns::sample_call(a
 int ns_sample_noalloc(const NsSampleArgs* args, void* stream) {
   using namespace ns;
   if (!args) return fail(NS_ERR_INVALID_ARG, "ns_sample_noalloc: args is NULL");
-  if (args->num_rows > NS_NOALLOC_MAX_ROWS)
-    return fail(NS_ERR_UNSUPPORTED, "ns_sample_noalloc: num_rows " + std::to_string(args->num_rows) +
-                                        " exceeds NS_NOALLOC_MAX_ROWS (" + std::to_string(NS_NOALLOC_MAX_ROWS) +
-                                        "), the rows its static scratch holds; use ns_sample for larger batches");
-  int dev = 0;
-  const cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail(NS_ERR_CUDA, std::string("ns_sample_noalloc: cudaGetDevice: ") + cudaGetErrorString(e));
-  std::string msg;
-  const int rc = rows_noalloc_setup(dev, msg);  // once per device (the current one)
-  if (rc != NS_OK) return fail(rc, "ns_sample_noalloc: " + msg);
   return sample_call(args, stream, true);
 }
 

@@ -3,14 +3,58 @@
 // A thin adapter: it checks devices/dtypes, turns tensors into raw pointers,
 // fills an NsSampleArgs and calls ns_sample() on the current CUDA stream.
 // No math happens here; the kernel lives in libnanoserve_sampler.so.
+//
+// Each (device, stream) gets its own workspace (NsSampleArgs.workspace),
+// zeroed once when it is allocated through torch's caching allocator and
+// left zero by every call, so calls on different streams never share one.
+// Warm a stream up before capturing a graph on it, so that the graph does
+// not hold the workspace's first zeroing.
 #include <ATen/core/Tensor.h>
+#include <ATen/ops/zeros.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 #include <torch/library.h>
 
+#include <mutex>
+#include <unordered_map>
+
 #include "../../include/nanoserve_sampler.h"
 
 namespace {
+
+struct Workspace {
+  at::Tensor t;
+  bool zero_pending = false;  // made during a stream capture: its zeroing ran only inside the graph
+};
+std::mutex g_ws_mu;
+// never destroyed: the tensors must not be freed after the CUDA context at exit
+auto* g_ws = new std::unordered_map<uint64_t, Workspace>();
+
+at::Tensor workspace_for(const at::Device& dev, cudaStream_t stream, int64_t bytes) {
+  const uint64_t key = (uint64_t)reinterpret_cast<uintptr_t>(stream) * 64u + (uint64_t)dev.index();
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  TORCH_CHECK(cudaStreamIsCapturing(stream, &cap) == cudaSuccess, "cudaStreamIsCapturing failed");
+  const bool capturing = cap != cudaStreamCaptureStatusNone;
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  auto it = g_ws->find(key);
+  if (it != g_ws->end() && it->second.t.numel() >= bytes) {
+    Workspace& w = it->second;
+    if (w.zero_pending && !capturing) {
+      // a graph made it and may never have been replayed: zero it before this eager call
+      TORCH_CHECK(cudaMemsetAsync(w.t.data_ptr(), 0, (size_t)w.t.numel(), stream) == cudaSuccess,
+                  "cudaMemsetAsync of the sampler workspace failed");
+      w.zero_pending = false;
+    }
+    return w.t;
+  }
+  // zeroed on the current stream, the one the kernel is enqueued on (inside a
+  // capture the zeroing becomes a node of the graph)
+  Workspace w;
+  w.t = at::zeros({bytes}, at::TensorOptions().dtype(at::kByte).device(dev));
+  w.zero_pending = capturing;
+  (*g_ws)[key] = w;
+  return w.t;
+}
 
 const void* opt_ptr(const c10::optional<at::Tensor>& t) {
   return (t.has_value() && t->defined()) ? t->data_ptr() : nullptr;
@@ -30,14 +74,14 @@ void check_opt(const c10::optional<at::Tensor>& t, const at::Device& dev, const 
 
 // sample(logits, sample_indices, row_params, history_offsets, history_ids,
 //        uniforms, philox_seed, philox_offset, row_offset, out,
-//        out_penalized, out_filtered, out_probs, status, row_order) -> ()
+//        out_penalized, out_filtered, out_probs, status, row_order, kernel) -> ()
 void sample_op(const at::Tensor& logits, const c10::optional<at::Tensor>& sample_indices,
                const at::Tensor& row_params, const c10::optional<at::Tensor>& history_offsets,
                const c10::optional<at::Tensor>& history_ids, const c10::optional<at::Tensor>& uniforms,
                int64_t philox_seed, int64_t philox_offset, int64_t row_offset, at::Tensor& out,
                const c10::optional<at::Tensor>& out_penalized, const c10::optional<at::Tensor>& out_filtered,
                const c10::optional<at::Tensor>& out_probs, const c10::optional<at::Tensor>& status,
-               const c10::optional<at::Tensor>& row_order) {
+               const c10::optional<at::Tensor>& row_order, int64_t kernel) {
   TORCH_CHECK(logits.dim() == 2, "logits must be 2-D [rows, vocab]");
   TORCH_CHECK(logits.is_cuda(), "logits must be a CUDA tensor");
   TORCH_CHECK(logits.stride(1) == 1, "logits rows must be contiguous");
@@ -97,7 +141,13 @@ void sample_op(const at::Tensor& logits, const c10::optional<at::Tensor>& sample
   a.out_probs = static_cast<float*>(const_cast<void*>(opt_ptr(out_probs)));
   a.status = static_cast<uint32_t*>(const_cast<void*>(opt_ptr(status)));
   a.row_order = static_cast<const int32_t*>(opt_ptr(row_order));
-  const int rc = ns_sample(&a, c10::cuda::getCurrentCUDAStream(dev.index()).stream());
+  a.kernel = (int32_t)kernel;
+  const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev.index()).stream();
+  const int64_t ws_bytes = ns_workspace_bytes((int32_t)S);
+  const at::Tensor ws = workspace_for(dev, stream, ws_bytes);
+  a.workspace = ws.data_ptr();
+  a.workspace_bytes = ws.numel();
+  const int rc = ns_sample(&a, stream);
   TORCH_CHECK(rc == NS_OK, "ns_sample failed (", rc, "): ", ns_last_error());
 }
 
@@ -108,7 +158,7 @@ TORCH_LIBRARY(nanoserve_b200, m) {
       "sample(Tensor logits, Tensor? sample_indices, Tensor row_params, Tensor? history_offsets, "
       "Tensor? history_ids, Tensor? uniforms, int philox_seed, int philox_offset, int row_offset, "
       "Tensor(a!) out, Tensor(b!)? out_penalized, Tensor(c!)? out_filtered, Tensor(d!)? out_probs, "
-      "Tensor(e!)? status, Tensor? row_order=None) -> ()");
+      "Tensor(e!)? status, Tensor? row_order=None, int kernel=0) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(nanoserve_b200, CUDA, m) { m.impl("sample", &sample_op); }

@@ -162,7 +162,7 @@ class HistoryStore:
             hb[o : o + p.nbytes] = p
         dev = host.to(self.device, non_blocking=True)
         ev = torch.cuda.Event()
-        ev.record()
+        ev.record(torch.cuda.current_stream(self.device))
         self._staging.event = ev
         row_params = dev[pos[0] : pos[0] + rows.nbytes]
         off_d = dev[pos[1] : pos[1] + offsets.nbytes].view(torch.int64)
@@ -194,7 +194,7 @@ class HistoryStore:
         host.numpy()[: dst.nbytes] = dst.view(np.uint8)
         dev = host[: dst.nbytes].to(self.device, non_blocking=True)
         ev = torch.cuda.Event()
-        ev.record()
+        ev.record(torch.cuda.current_stream(self.device))
         self._append_staging.event = ev
         tokens = tokens.contiguous()
         _cabi.ns_history_append(self.pool.data_ptr(), self.capacity, dev.data_ptr(), tokens.data_ptr(),
@@ -206,9 +206,16 @@ class HistoryStore:
     def sample(self, sampler: Sampler, logits: torch.Tensor, sampling_params_list: Sequence, handles: Sequence[int],
                *, append: bool = True, **kw):
         """``Sampler.sample`` with the histories taken from this store; the
-        sampled ids are appended to the requests' histories (``append``)."""
-        rp, off, ids, order = self.pack(sampling_params_list, handles, sms=_sm_count(logits.device))
-        out = sampler.sample_packed(logits, rp, off, ids, row_order=order, **kw)
-        if append:
-            self.append(handles, out[0] if isinstance(out, tuple) else out)
-        return out
+        sampled ids are appended to the requests' histories (``append``).
+        Runs on the store's device (whatever device is current) inside an NVTX
+        range named ``logits+sample`` (nanoserve/engine/engine.py:234)."""
+        torch.cuda.nvtx.range_push("logits+sample")
+        try:
+            with torch.cuda.device(self.device):
+                rp, off, ids, order = self.pack(sampling_params_list, handles, sms=_sm_count(logits.device))
+                out = sampler.sample_packed(logits, rp, off, ids, row_order=order, **kw)
+                if append:
+                    self.append(handles, out[0] if isinstance(out, tuple) else out)
+                return out
+        finally:
+            torch.cuda.nvtx.range_pop()

@@ -14,8 +14,13 @@ which filters run are made here exactly as the reference makes them:
   must lie in ``[0, vocab)``; otherwise ``IndexError`` is raised, as the
   reference's ``index_select`` does (sampler.py:35).
 
+A request with a ``seed`` (nanoserve/config.py:79, which the reference
+ignores) gets its own Philox key and, as the counter, the length of its
+history (prompt plus tokens so far): the same request in the same state
+draws the same number whatever batch it is in.
+
 It also builds the optional row order (``NsSampleArgs.row_order``), a
-scheduling hint that spreads the expensive rows over the GPU's SMs.
+scheduling hint that starts the rows with the longest finishing work first.
 """
 from __future__ import annotations
 
@@ -34,7 +39,7 @@ ROW_DTYPE = np.dtype(
         ("repetition_penalty", "<f4"),
         ("top_k", "<i4"),
         ("flags", "<u4"),
-        ("reserved", "<u4"),
+        ("seed_step", "<u4"),
         ("seed", "<u8"),
     ]
 )
@@ -57,11 +62,13 @@ def derive_row(p, vocab: int, hist_len: int) -> tuple:
         flags |= _cabi.NS_ROW_PENALTY
     seed = getattr(p, "seed", None)
     seed_u64 = 0
+    step = 0
     if seed is not None:
         flags |= _cabi.NS_ROW_SEED
         seed_u64 = int(seed) & 0xFFFFFFFFFFFFFFFF
+        step = int(hist_len) & 0xFFFFFFFF
     top_p32 = np.float32(p.top_p) if p.top_p < 1.0 else np.float32(1.0)
-    return (np.float32(temp), top_p32, np.float32(rp), k_eff, flags, 0, seed_u64)
+    return (np.float32(temp), top_p32, np.float32(rp), k_eff, flags, step, seed_u64)
 
 
 def derive_rows(params: Sequence, vocab: int, hist_lens) -> np.ndarray:
@@ -85,22 +92,24 @@ def derive_rows(params: Sequence, vocab: int, hist_lens) -> np.ndarray:
     rows["top_k"] = [int(k) if (k > 0 and k < vocab) else 0 for k in (p.top_k for p in params)]
     seeds = [getattr(p, "seed", None) for p in params]
     if any(sd is not None for sd in seeds):
-        flags |= np.array([_cabi.NS_ROW_SEED if sd is not None else 0 for sd in seeds])
+        seeded = np.array([sd is not None for sd in seeds])
+        flags |= np.where(seeded, _cabi.NS_ROW_SEED, 0)
         rows["seed"] = [int(sd) & 0xFFFFFFFFFFFFFFFF if sd is not None else 0 for sd in seeds]
+        rows["seed_step"] = np.where(seeded, lens & 0xFFFFFFFF, 0).astype(np.uint32)
     rows["flags"] = flags
     return rows
 
 
-# Relative cost of a row on the one-block-per-row kernel, by the path it
-# takes there (greedy; top-k <= 128 with or without top-p; top-p alone, large
-# top-k or plain sampling), from measured single-row times on B200.
+# Relative length of a row's finishing work on the split-row kernel (the
+# block that summarises its last part finishes it): greedy rows only merge
+# numbers, top-k <= 128 rows sort a short candidate list, plain sampling and
+# top-p rows re-read the row, large top-k rows re-read it several times.
 TOPK_LIST_MAX = 128
 COST_GREEDY, COST_TOPK, COST_PLAIN, COST_TOPP, COST_LARGE_K = 1, 3, 5, 7, 8
-ROWS_PER_SM = 2  # resident blocks per SM of the one-block-per-row kernel
 
 
 def row_costs(row_params: np.ndarray) -> np.ndarray:
-    """Cost class of every packed row (larger = longer on its SM)."""
+    """Cost class of every packed row (larger = longer finishing work)."""
     flags = row_params["flags"]
     k = row_params["top_k"]
     greedy = (flags & _cabi.NS_ROW_GREEDY) != 0
@@ -113,33 +122,20 @@ def row_costs(row_params: np.ndarray) -> np.ndarray:
     return cost
 
 
-def schedule(row_params: np.ndarray, sms: int, per_sm: int = ROWS_PER_SM) -> np.ndarray:
-    """Row order for ``NsSampleArgs.row_order``.
+def schedule(row_params: np.ndarray, sms: int) -> np.ndarray:
+    """Row order for ``NsSampleArgs.row_order``: the most expensive rows first.
 
-    The row kernel's block b takes positions b, b + G, b + 2G, ... of the
-    order (G = min(S, per_sm * sms) blocks, per_sm of them on each SM).
-    Each round of G positions gives the first sms blocks, which the hardware
-    spreads one per SM, the most expensive rows left, and the other blocks
-    the cheapest left, so that expensive rows do not pile up on few SMs.
+    The split-row kernel hands out the parts of row position 0 first, then
+    those of position 1, and so on; a row's finishing work runs as soon as its
+    last part is summarised, while later rows stream.  Putting the rows with
+    the longest finishing work first lets that work overlap the streaming of
+    the cheap rows, which end the step.  (``sms`` only says that the caller
+    has a GPU to schedule for; the order does not depend on its size.)
     """
     S = row_params.shape[0]
-    order = np.arange(S, dtype=np.int32)
     if S == 0 or sms <= 0:
-        return order
-    by_cost = np.argsort(-row_costs(row_params), kind="stable").astype(np.int32)
-    G = min(S, per_sm * sms)
-    lo, hi, t = 0, S, 0
-    while t < S:
-        n = min(G, S - t)
-        n1 = min(n, sms)
-        n2 = n - n1
-        order[t : t + n1] = by_cost[lo : lo + n1]
-        lo += n1
-        if n2:
-            order[t + n1 : t + n] = by_cost[hi - n2 : hi][::-1]
-            hi -= n2
-        t += n
-    return order
+        return np.arange(S, dtype=np.int32)
+    return np.argsort(-row_costs(row_params), kind="stable").astype(np.int32)
 
 
 @dataclass

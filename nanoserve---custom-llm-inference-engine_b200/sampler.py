@@ -5,8 +5,9 @@ generators=None)`` keeps the reference signature (sampler.py:17-27) and
 returns int64 token ids on ``logits.device``, so ``engine.py:247-250`` and
 ``Scheduler.update_with_sampled`` work unchanged.  The work is one call of
 the sm_100a library behind ``torch.ops.nanoserve_b200.sample``: one kernel
-launch, or two (a top-p pre-pass, then the row kernel) for batches of at most
-256 rows.
+launch, enqueued on the current stream of ``logits.device``.  The call is
+wrapped in an NVTX range named ``logits+sample``, the range the reference's
+engine opens around the same step (nanoserve/engine/engine.py:234).
 
 Differences from the reference, all additive:
 
@@ -18,7 +19,9 @@ Differences from the reference, all additive:
 * randomness comes from per-row Philox4x32-10 streams keyed by
   ``(seed, step, row)`` instead of the global generator that
   ``torch.multinomial`` uses (sampler.py:87); ``SamplingParams.seed``, which
-  the reference ignores, gives a row its own key;
+  the reference ignores, gives a request its own stream, keyed by the seed
+  and the length of its history, so it draws the same tokens whatever batch
+  it is in;
 * ``generators`` is accepted and ignored, as in the reference (sampler.py:26);
 * ``sample_async`` returns int32 ids through a non-blocking copy to pinned
   host memory (``PendingTokens.wait()``), in place of the caller's blocking
@@ -114,19 +117,30 @@ class _HostRing:
             self._bufs[i] = torch.empty(max(n, 1024), dtype=torch.int32, pin_memory=True)
         host = self._bufs[i]
         src = tokens if tokens.dtype == torch.int32 else tokens.to(torch.int32)
-        host[:n].copy_(src, non_blocking=True)
-        ev = torch.cuda.Event()
-        ev.record()
+        with torch.cuda.device(tokens.device):
+            host[:n].copy_(src, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(tokens.device))
         pt = PendingTokens(host, ev, n)
         self._pending[i] = pt
         return pt
 
 
-class Sampler:
-    """B200 sampling op with the reference ``Sampler`` interface."""
+KERNELS = {"auto": 0, "cluster": 1, "split": 2}
 
-    def __init__(self, device):
+
+class Sampler:
+    """B200 sampling op with the reference ``Sampler`` interface.
+
+    ``kernel`` picks the CUDA kernel: ``"auto"`` (the split-row kernel for
+    batches of at least 32 aligned rows, the cluster kernel otherwise),
+    ``"cluster"`` or ``"split"`` (where its layout conditions hold)."""
+
+    def __init__(self, device, kernel: str = "auto"):
+        if kernel not in KERNELS:
+            raise ValueError(f"kernel must be one of {sorted(KERNELS)}")
         self.device = torch.device(device)
+        self.kernel = kernel
         self._step = 0
         self._staging = _Staging()
         self._ring = _HostRing()
@@ -172,13 +186,21 @@ class Sampler:
         S = len(sampling_params_list)
         if sample_indices is None and logits.shape[0] != S:
             raise ValueError(f"logits has {logits.shape[0]} rows but {S} sampling params were given")
-        packed = packing.pack(sampling_params_list, history_token_ids, vocab, sms=_sm_count(logits.device))
-        row_params, offsets, ids, order = self._upload(packed, logits.device)
-        return self.sample_packed(
-            logits, row_params, offsets, ids,
-            sample_indices=sample_indices, uniforms=uniforms, seed=seed,
-            out_dtype=out_dtype, return_debug=return_debug, row_order=order,
-        )
+        torch.cuda.nvtx.range_push("logits+sample")
+        try:
+            # every copy, event and launch below goes to the logits' device,
+            # whatever device is current for the caller
+            with torch.cuda.device(logits.device):
+                packed = packing.pack(sampling_params_list, history_token_ids, vocab,
+                                      sms=_sm_count(logits.device))
+                row_params, offsets, ids, order = self._upload(packed, logits.device)
+                return self.sample_packed(
+                    logits, row_params, offsets, ids,
+                    sample_indices=sample_indices, uniforms=uniforms, seed=seed,
+                    out_dtype=out_dtype, return_debug=return_debug, row_order=order,
+                )
+        finally:
+            torch.cuda.nvtx.range_pop()
 
     # -- pre-packed device inputs (graph-capturable) ------------------------
     def sample_packed(
@@ -226,7 +248,7 @@ class Sampler:
             logits, sample_indices, row_params, history_offsets, history_ids, uniforms,
             int(seed) & 0x7FFFFFFFFFFFFFFF, int(offset), int(row_offset), out,
             dbg["penalized"] if dbg else None, dbg["filtered"] if dbg else None,
-            dbg["probs"] if dbg else None, dbg["status"] if dbg else None, row_order,
+            dbg["probs"] if dbg else None, dbg["status"] if dbg else None, row_order, KERNELS[self.kernel],
         )
         if return_debug:
             return out, dbg
@@ -238,7 +260,7 @@ class Sampler:
         packing.to_bytes(packed, host.numpy())
         dev = host.to(device, non_blocking=True)
         ev = torch.cuda.Event()
-        ev.record()
+        ev.record(torch.cuda.current_stream(device))
         self._staging.event = ev
         row_params = dev[a : a + packed.row_params.nbytes]
         offsets = dev[b : b + packed.offsets.nbytes].view(torch.int64)

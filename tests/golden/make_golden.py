@@ -1,7 +1,8 @@
 """Golden vectors from the REFERENCE sampler (run in the build container only).
 
-Imports ``nanoserve.scheduler.sampler.Sampler`` from the reference tree
-(default ``/root/reference``, or ``$NANOSERVE_REF``), runs it on CPU torch on
+Imports ``nanoserve.scheduler.sampler.Sampler`` from a reference checkout
+(``--ref PATH``, else ``$NANOSERVE_REF``; one of them is required), runs it
+on CPU torch on
 every case of ``cases.py`` and stores, per row, what the reference leaves
 observable:
 
@@ -14,7 +15,7 @@ observable:
 * inverse-CDF tokens for 8 more uniforms per row.
 
 Large arrays are stored as hashes plus values at probe indices, so the
-fixture stays small.  Usage: ``python tests/golden/make_golden.py``.
+fixture stays small.  Usage: ``python tests/golden/make_golden.py --ref PATH``.
 """
 from __future__ import annotations
 
@@ -29,7 +30,7 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
 import cases as C  # noqa: E402
 
-REF = Path(os.environ.get("NANOSERVE_REF", "/root/reference"))
+REF = None  # the reference checkout, set by main()
 
 
 def load_reference():
@@ -147,4 +148,13 @@ def main() -> None:
 
 
 if __name__ == "__main__":
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.environ.get("NANOSERVE_REF"),
+                    help="reference checkout (default: $NANOSERVE_REF)")
+    ref = ap.parse_args().ref
+    if not ref:
+        ap.error("give the reference checkout with --ref or $NANOSERVE_REF")
+    REF = Path(ref)
     main()

@@ -27,7 +27,8 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_limits():
     lib = cabi.load_library()
-    assert lib.ns_abi_version() == 2
+    assert lib.ns_abi_version() == cabi.NS_ABI_VERSION == 3
+    assert cabi.ns_workspace_bytes(1) == cabi.ns_workspace_bytes(16384) == cabi.NS_NOALLOC_WORKSPACE_BYTES
     assert lib.ns_max_vocab(cabi.NS_DTYPE_F32) >= 151936  # Llama-3 (128256) and Qwen-2 vocabularies
 
 

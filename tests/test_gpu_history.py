@@ -77,22 +77,21 @@ def test_append_extends_each_history():
     assert int(st.status.item()) == 0
 
 
-@pytest.mark.parametrize("path", ["rows", "cluster"])
-def test_sampling_through_the_store_matches_lists(path, monkeypatch):
+@pytest.mark.parametrize("path", ["split", "cluster"])
+def test_sampling_through_the_store_matches_lists(path):
     """Three decode steps: Sampler.sample over Python lists (the reference's
     calling convention, engine.py:242-249) against HistoryStore.sample; the
     lists grow by the sampled ids, the store by its own appends."""
-    monkeypatch.setenv("NS_SAMPLE_PATH", path)
     dev = _dev()
     V = 128256
     rng = np.random.default_rng(23)
-    S = 64 if path == "rows" else 12
+    S = 64 if path == "split" else 12
     params = W.mixed_params(S)
     params = [SP(temperature=p.temperature, top_k=p.top_k, top_p=p.top_p,
                  repetition_penalty=1.3 if i % 3 == 0 else p.repetition_penalty) for i, p in enumerate(params)]
     hists = W.histories(rng, S, 0, 600, V)
     st, handles = _fragmented_store(dev, V, [list(h) for h in hists], extra=8)
-    s_list, s_store = NS.Sampler(dev), NS.Sampler(dev)
+    s_list, s_store = NS.Sampler(dev, kernel=path), NS.Sampler(dev, kernel=path)
     for step in range(3):
         x = (rng.standard_normal((S, V)) * 2.0).astype(np.float32)
         for r in range(S):  # make the penalty decide: boost a few prior ids

@@ -20,10 +20,10 @@ pytestmark = pytest.mark.gpu
 W = importlib.import_module(H.PKG + ".workloads")
 
 
-@pytest.fixture(params=["cluster", "rows"], autouse=True)
+@pytest.fixture(params=["cluster", "split"], autouse=True)
 def sample_path(request, monkeypatch):
-    """Run every test through both kernels (rows only where its layout holds)."""
-    monkeypatch.setenv("NS_SAMPLE_PATH", request.param)
+    """Run every test through both kernels (split only where its layout holds)."""
+    monkeypatch.setitem(H.KERNEL, "name", request.param)
     return request.param
 
 
@@ -44,6 +44,36 @@ def test_config_parity(config, rows):
     gpu = H.run_cabi(lg, w.params, w.histories, w.uniforms, sample_indices=w.sample_indices)
     assert gpu["status"] == 0
     rep = H.compare(gpu, w.gathered(), w.params, w.histories, w.uniforms)
+    print(f"config {config}: rows {rep.rows}, top-p band {rep.topp_band_rows}, draw band {rep.draw_band_rows}")
+    _check(rep)
+
+
+_FULL = {}
+
+
+def _full_size(config: int):
+    """Config 4 at its 1024 rows, or a 1024-row slice of config 5 (every
+    parameter kind, histories U[128,1024]), with the oracle's results."""
+    if config not in _FULL:
+        w = W.make(config, rows=1024, seed=50 + config)
+        _FULL[config] = (w, H.oracle_rows(w.gathered(), w.params, w.histories, w.uniforms))
+    return _FULL[config]
+
+
+@pytest.mark.parametrize("debug", [False, True])
+@pytest.mark.parametrize("config", [4, 5])
+def test_full_size_batches(config, debug):
+    """More than twice as many rows as the GPU has SMs in one call, so every
+    persistent block of either kernel takes many rows (and the split-row
+    kernel reuses its workspace slots): bit-exact penalised and filtered
+    logits, |dp| <= 1e-6 and the oracle's tokens (debug on), the oracle's
+    tokens (debug off)."""
+    dev = _dev()
+    w, expected = _full_size(config)
+    lg = torch.from_numpy(w.logits).to(dev)
+    gpu = H.run_cabi(lg, w.params, w.histories, w.uniforms, sample_indices=w.sample_indices, debug=debug)
+    assert gpu["status"] == 0
+    rep = H.compare(gpu, w.gathered(), w.params, w.histories, w.uniforms, expected=expected)
     print(f"config {config}: rows {rep.rows}, top-p band {rep.topp_band_rows}, draw band {rep.draw_band_rows}")
     _check(rep)
 
@@ -266,13 +296,10 @@ def test_row_order_changes_nothing_but_the_schedule():
     assert np.array_equal(got["tokens"], base["tokens"])
 
 
-@pytest.mark.parametrize("prepass", ["1", "0"])
 @pytest.mark.parametrize("V", [32768, 128256])
-def test_top_p_rows_without_debug_outputs(V, prepass, monkeypatch):
-    """The production path (no debug outputs): top-p rows may stream their
-    first pass through the split pre-pass, which must give the oracle's
-    tokens like the single-block path does (NS_PREPASS=0)."""
-    monkeypatch.setenv("NS_PREPASS", prepass)
+def test_top_p_rows_without_debug_outputs(V):
+    """The production path (no debug outputs): top-p rows are finished from
+    their parts' histograms and give the oracle's tokens."""
     dev = _dev()
     rng = np.random.default_rng(44)
     SP = importlib.import_module(H.PKG + ".config").SamplingParams
@@ -296,12 +323,9 @@ def test_top_p_rows_without_debug_outputs(V, prepass, monkeypatch):
     _check(H.compare(gpu, np.stack(rows), params, hists, u))
 
 
-@pytest.mark.parametrize("prepass", ["1", "0"])
-def test_config3_bf16_gather_without_debug_outputs(prepass, monkeypatch):
+def test_config3_bf16_gather_without_debug_outputs():
     """Config 3 as served (64 gathered bf16 rows, top-p 0.95, penalty 1.2, no
-    debug outputs): the bf16 pre-pass and the single-block path both give
-    the oracle's tokens."""
-    monkeypatch.setenv("NS_PREPASS", prepass)
+    debug outputs) gives the oracle's tokens."""
     dev = _dev()
     w = W.make(3, seed=34)
     lg = H.to_bf16_tensor(w.logits, dev)

@@ -14,10 +14,10 @@ NS = importlib.import_module(H.PKG)
 W = importlib.import_module(H.PKG + ".workloads")
 
 
-@pytest.fixture(params=["cluster", "rows"], autouse=True)
+@pytest.fixture(params=["cluster", "split"], autouse=True)
 def sample_path(request, monkeypatch):
-    """Run every test through both kernels (rows only where its layout holds)."""
-    monkeypatch.setenv("NS_SAMPLE_PATH", request.param)
+    """Run every test through both kernels (split only where its layout holds)."""
+    monkeypatch.setitem(H.KERNEL, "name", request.param)
     return request.param
 
 
@@ -30,7 +30,7 @@ def test_sampler_drop_in_signature_and_results():
     dev = _dev()
     w = W.make(2, rows=32, seed=21)
     lg = torch.from_numpy(w.logits).to(dev)
-    s = NS.Sampler(dev)
+    s = H.make_sampler(dev)
     out = s.sample(lg, w.params, w.histories)  # the reference call, engine.py:247-249
     assert out.dtype == torch.int64 and out.shape == (32,) and out.device == lg.device
     toks = out.tolist()  # engine.py:250
@@ -54,7 +54,7 @@ def test_sampler_accepts_reference_sampling_params_objects():
         temperature, top_p, top_k, repetition_penalty, seed = 0.0, 1.0, -1, 1.0, None
 
     lg = torch.randn(2, 1000, device=dev)
-    out = NS.Sampler(dev).sample(lg, [Ref(), Ref()], [[], []])
+    out = H.make_sampler(dev).sample(lg, [Ref(), Ref()], [[], []])
     assert out.tolist() == torch.argmax(lg, dim=-1).tolist()
 
 
@@ -64,7 +64,7 @@ def test_sampler_gather_and_bf16():
     lg = H.to_bf16_tensor(w.logits, dev)
     idx = torch.from_numpy(w.sample_indices).to(dev)
     uni = torch.from_numpy(w.uniforms).to(dev)
-    out, dbg = NS.Sampler(dev).sample(lg, w.params, w.histories, sample_indices=idx, uniforms=uni,
+    out, dbg = H.make_sampler(dev).sample(lg, w.params, w.histories, sample_indices=idx, uniforms=uni,
                                       return_debug=True)
     gpu = dict(tokens=out.cpu().numpy(), penalized=dbg["penalized"].cpu().numpy(),
                filtered=dbg["filtered"].cpu().numpy(), probs=dbg["probs"].cpu().numpy())
@@ -77,7 +77,7 @@ def test_sampler_rejects_bad_history_like_the_reference():
     lg = torch.randn(1, 100, device=dev)
     p = NS.SamplingParams(temperature=1.0, repetition_penalty=1.2)
     with pytest.raises(IndexError):
-        NS.Sampler(dev).sample(lg, [p], [[5, 100]])
+        H.make_sampler(dev).sample(lg, [p], [[5, 100]])
 
 
 def test_sampler_graph_capture():
@@ -85,7 +85,7 @@ def test_sampler_graph_capture():
     dev = _dev()
     w = W.make(2, rows=16, seed=41)
     lg = torch.from_numpy(w.logits).to(dev)
-    s = NS.Sampler(dev)
+    s = H.make_sampler(dev)
     pk = H.packing.pack(w.params, w.histories, lg.shape[1])
     rp, off, ids, _ = importlib.import_module(H.PKG + ".sampler").upload_packed(pk, dev)
     out = torch.empty(16, dtype=torch.int64, device=dev)
@@ -125,7 +125,7 @@ def test_draw_distribution_chi_square(kind):
     idx = torch.zeros(R, dtype=torch.int64, device=dev)
     pk = H.packing.pack([p] * R, [[]] * R, V)
     rp = torch.from_numpy(pk.row_params.view(np.uint8).copy()).to(dev)
-    s = NS.Sampler(dev)
+    s = H.make_sampler(dev)
     counts = torch.zeros(V, dtype=torch.int64, device=dev)
     out = torch.empty(R, dtype=torch.int64, device=dev)
     for k in range(reps):
@@ -147,3 +147,37 @@ def test_draw_distribution_chi_square(kind):
     pval = chi2.sf(stat, dof)
     print(f"{kind}: {int(n)} draws, {dof} dof, chi2 {stat:.1f}, p {pval:.3g}")
     assert pval > 1e-3
+
+
+def test_seeded_requests_are_reproducible():
+    """A request with a seed (nanoserve/config.py:79) draws the same token in
+    the same state whatever batch it is in, wherever it sits in it and however
+    many calls the sampler has made; other seeds draw other tokens."""
+    dev = _dev()
+    V = 32768
+    rng = np.random.default_rng(91)
+    x = W.peaked_logits(rng, 1, V)[0]
+    hist = rng.integers(0, V, 300).tolist()
+
+    def req(seed):
+        return NS.SamplingParams(temperature=1.0, top_p=0.95, repetition_penalty=1.1, seed=seed)
+
+    def batch(n_other, pos, seed, warm_calls):
+        others = W.peaked_logits(rng, n_other, V)
+        rows = np.insert(others, pos, x, axis=0)
+        params = W.mixed_params(n_other)
+        params.insert(pos, req(seed))
+        hists = W.histories(rng, n_other, 0, 200, V)
+        hists.insert(pos, hist)
+        s = H.make_sampler(dev)
+        lg = torch.from_numpy(rows).to(dev)
+        for _ in range(warm_calls):
+            s.sample(lg, params, hists)
+        return int(s.sample(lg, params, hists)[pos].item())
+
+    a = batch(7, 0, 1234, 0)
+    b = batch(40, 23, 1234, 3)
+    c = batch(63, 63, 1234, 1)
+    assert a == b == c
+    others = {batch(7, 0, sd, 0) for sd in range(16)}
+    assert len(others) > 1

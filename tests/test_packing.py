@@ -92,25 +92,39 @@ def test_row_params_byte_layout():
     assert raw[24:32].view(np.uint64)[0] == 9
 
 
-def test_schedule_is_a_permutation_that_spreads_expensive_rows():
+def test_schedule_puts_the_longest_finishing_work_first():
     W = importlib.import_module(PKG_NAME + ".workloads")
     sms = 148
     for S in (1, 7, 148, 256, 296, 1000):
         pk = packing.pack(W.mixed_params(S), [[]] * S, V, sms=sms)
         order = pk.order
         assert order.dtype == np.int32 and sorted(order.tolist()) == list(range(S))
-    # config 2: blocks b and b + sms share an SM; no SM gets two top-p rows,
-    # and every top-p row shares its SM with the cheapest rows there are
+        cost = packing.row_costs(pk.row_params)[order]
+        assert (np.diff(cost) <= 0).all()  # non-increasing cost along the order
+    # config 2: the 64 top-p rows first, the 64 greedy rows last, ties in row order
     pk = packing.pack(W.mixed_params(256), [[]] * 256, V, sms=sms)
     cost = packing.row_costs(pk.row_params)[pk.order]
-    pair = cost[:sms].copy()
-    pair[: 256 - sms] += cost[sms:]
-    assert pair.max() <= packing.COST_TOPP + packing.COST_GREEDY
-    assert (cost[:64] == packing.COST_TOPP).all()
+    assert (cost[:64] == packing.COST_TOPP).all() and (cost[-64:] == packing.COST_GREEDY).all()
+    assert pk.order[:64].tolist() == list(range(2, 256, 4))
     # without an SM count there is no order; layout then has an empty order region
     pk = packing.pack(W.mixed_params(8), [[]] * 8, V)
     a, b, c, d, end = packing.layout(pk)
     assert pk.order is None and end >= d
+
+
+def test_seeded_rows_carry_their_history_length_as_the_counter():
+    """NS_ROW_SEED rows: key = the request's seed, counter = its history length
+    (prompt + tokens so far), so the stream does not depend on the batch."""
+    ps = [SP(temperature=1.0, seed=5), SP(temperature=1.0), SP(temperature=0.5, seed=2**64 + 3)]
+    hs = [[1, 2, 3], [4] * 9, list(range(70000))]
+    pk = packing.pack(ps, hs, 100000)
+    r = pk.row_params
+    assert (r["flags"][[0, 2]] & cabi.NS_ROW_SEED).all() and not (r["flags"][1] & cabi.NS_ROW_SEED)
+    assert r["seed_step"].tolist() == [3, 0, 70000]
+    assert r["seed"].tolist() == [5, 0, 3]
+    for i in range(3):
+        one = packing.derive_row(ps[i], 100000, len(hs[i]))
+        assert one[5] == r["seed_step"][i] and one[6] == r["seed"][i]
 
 
 def test_order_travels_in_the_staging_buffer():
