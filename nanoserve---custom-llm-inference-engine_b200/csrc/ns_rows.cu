@@ -56,7 +56,9 @@ constexpr int kChunkTarget = 32768;           // bytes per chunk (rounded to who
 constexpr int kMaxChunksRow = 32;             // chunks per row at most
 constexpr int kUnit = 32;                     // chunk boundaries fall on multiples of 32 elements
 constexpr int kRingMax = 8;                   // ring slots at most
-constexpr int kRefreshChunk = 2;              // TOPK: the bound is refreshed after this chunk
+constexpr int kRefreshChunk = 2;              // TOPK: the bound is refreshed after this chunk ...
+constexpr int kRefreshMinK = 64;              // ... when k exceeds this: the bound from chunk 0 leaves
+                                              // about k * chunks candidates, which fits kCandCap below it
 constexpr long long kSpinLimit = 1ll << 22;   // bounded waits (a few seconds at most)
 
 // ---------------------------------------------------------------- global workspace
@@ -94,7 +96,7 @@ struct Geo {
   int nchunk, units;   // chunks per row, 32-element units per row
   int nslot;           // ring slots
   int slot_bytes;      // bytes per ring slot (the largest chunk)
-  int ppc;             // second-pass pieces (32 slots) per chunk
+  int ppc;             // second-pass pieces (kPieceSlots slots) per chunk, at most kWarps
   int o_ctl, o_bitmap, o_hist, o_cand, o_small, o_ring, smem;
 };
 
@@ -274,34 +276,36 @@ __device__ __forceinline__ void track_max(RowAcc& acc, const float (&x)[E::kEPT]
 // kRounds independent chains of work, so the few warps of a block keep
 // enough instructions in flight.
 constexpr int kRounds = 4;
+constexpr int kPieceSlots = 32 * kRounds;  // slots of a second-pass piece (one warp's share of a chunk)
 
 template <class E>
 struct Batch {
   typename E::Raw raw[kRounds];
 };
 
-template <class E>
-__device__ __forceinline__ void load_batch(const unsigned char* tile, int j0, int nsl, Batch<E>& b) {
-#pragma unroll
-  for (int r = 0; r < kRounds; ++r) {
-    const int j = j0 + r * kThreads;
-    b.raw[r] = j < nsl ? E::lds(tile + (size_t)j * 16) : E::zero();
-  }
+__device__ __forceinline__ void red_add_shared(uint32_t addr, uint32_t v) {
+  asm volatile("red.shared.add.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
 
-// The same, with slots past the chunk read as -inf logits (no mass, never a
-// member), so that the work on a batch needs no liveness tests.
+// Element q of a thread's slot (an unrolled select: a register array indexed
+// at run time would live in local memory).
+template <int N>
+__device__ __forceinline__ float pick(const float (&x)[N], int q) {
+  float v = x[0];
+#pragma unroll
+  for (int i = 1; i < N; ++i) v = (q == i) ? x[i] : v;
+  return v;
+}
+
+// (shared-space loads: the ring's address reaches these loops as a generic
+// pointer, and generic loads of shared memory cost more latency)
 template <class E>
-__device__ __forceinline__ void load_batch_ninf(const unsigned char* tile, int j0, int nsl, Batch<E>& b) {
+__device__ __forceinline__ void load_batch(const unsigned char* tile, int j0, int nsl, Batch<E>& b) {
+  const uint32_t t = smem_addr(tile);
 #pragma unroll
   for (int r = 0; r < kRounds; ++r) {
     const int j = j0 + r * kThreads;
-    if (j < nsl) {
-      b.raw[r] = E::lds(tile + (size_t)j * 16);
-    } else {
-      uint4 ninf = make_uint4(E::kNegInf2, E::kNegInf2, E::kNegInf2, E::kNegInf2);
-      b.raw[r] = *reinterpret_cast<const typename E::Raw*>(&ninf);
-    }
+    b.raw[r] = j < nsl ? E::lds_s(t + (uint32_t)j * 16u) : E::zero();
   }
 }
 
@@ -329,6 +333,7 @@ __device__ __forceinline__ void max_pass(const unsigned char* tile, const uint32
 template <class E, bool PEN, bool TONE, bool HIST, bool TRACK>
 __device__ __forceinline__ void mass_pass(const unsigned char* tile, const uint32_t* bitmap, uint32_t* hist, Pen pp,
                                           float T, float rT, float m0, int e_lo, int nsl, int tid, RowAcc& acc) {
+  const uint32_t hs = smem_addr(hist);
   for (int j0 = tid; j0 < nsl; j0 += kRounds * kThreads) {
     Batch<E> b;
     load_batch<E>(tile, j0, nsl, b);
@@ -348,7 +353,7 @@ __device__ __forceinline__ void mass_pass(const unsigned char* tile, const uint3
           if (HIST) {
             // no range test: e >= 2^32 and e < 2^-32 both clamp into the last bucket
             const uint32_t bits = __float_as_uint(e);
-            atomicAdd(&hist[min((kTopFine - bits) >> kShFine, (uint32_t)(kBins - 1))], approx_mass13(bits));
+            red_add_shared(hs + 4u * min((kTopFine - bits) >> kShFine, (uint32_t)(kBins - 1)), approx_mass13(bits));
           }
         }
         acc.lz += (double)part;
@@ -358,42 +363,42 @@ __device__ __forceinline__ void mass_pass(const unsigned char* tile, const uint3
 }
 
 // TOPK candidates: every element >= tau, as rank keys, appended to the
-// row's list (sh.cand; one shared atomic per warp round; entries past
+// row's list (sh.cand; one shared atomic per candidate: candidates are few,
+// and warp-wide appends cost more in collectives than they save; entries past
 // kCandCap are counted but dropped); with TRACK the maximum bookkeeping rides
-// along.
+// along.  A bit mask marks a batch's candidates, which a short loop re-reads
+// from the ring.
 template <class E, bool PEN, bool TRACK>
 __device__ __forceinline__ void cand_pass(const unsigned char* tile, const Sh& sh, Ring& rg, Pen pp, float tau,
                                           bool t_one, float T, float rT, int e_lo, int nsl, int tid, RowAcc& acc) {
-  const int lane = tid & 31;
-  // whole batches in every lane: the warp stays converged for its collectives
-  const int jend = (nsl + kRounds * kThreads - 1) / (kRounds * kThreads) * (kRounds * kThreads);
-  for (int j0 = tid; j0 < jend; j0 += kRounds * kThreads) {
+  constexpr int EPT = E::kEPT;
+  static_assert(kRounds * EPT <= 32, "one candidate bit per element of a batch");
+  const uint32_t ts = smem_addr(tile);
+  for (int j0 = tid; j0 < nsl; j0 += kRounds * kThreads) {
     Batch<E> b;
     load_batch<E>(tile, j0, nsl, b);
+    uint32_t memb = 0u;
 #pragma unroll
     for (int r = 0; r < kRounds; ++r) {
       const int j = j0 + r * kThreads;
       const bool live = j < nsl;
-      float x[E::kEPT];
-      penalized<E, PEN>(sh.bitmap, pp, b.raw[r], e_lo + j * E::kEPT, x, live);
-      if (TRACK && live) track_max<E>(acc, x, e_lo + j * E::kEPT);
-      uint32_t m = 0u;
+      float x[EPT];
+      penalized<E, PEN>(sh.bitmap, pp, b.raw[r], e_lo + j * EPT, x, live);
+      if (TRACK && live) track_max<E>(acc, x, e_lo + j * EPT);
 #pragma unroll
-      for (int q = 0; q < E::kEPT; ++q) m |= (live && x[q] >= tau) ? (1u << q) : 0u;
-      if (!__any_sync(0xffffffffu, m != 0u)) continue;
-      // one slot range for the warp's candidates of this round
-      const uint32_t cnt = (uint32_t)__popc(m);
-      const uint32_t incl = warp_incl_u32(cnt, lane);
-      uint32_t base = 0u;
-      if (lane == 31) base = atomicAdd(&rg.nlist, incl);
-      base = __shfl_sync(0xffffffffu, base, 31) + incl - cnt;
-      while (m) {
-        const int q = __ffs(m) - 1;
-        m &= m - 1u;
-        const float sv = t_one ? x[q] : div_by_const(x[q], T, rT);
-        if (base < (uint32_t)kCandCap) sh.cand[base] = rank_key(sv, e_lo + j * E::kEPT + q);
-        ++base;
-      }
+      for (int q = 0; q < EPT; ++q) memb |= (live && x[q] >= tau) ? (1u << (r * EPT + q)) : 0u;
+    }
+    while (memb) {
+      const int bit = __ffs(memb) - 1;
+      memb &= memb - 1u;
+      const int r = bit / EPT, q = bit % EPT;
+      const int j = j0 + r * kThreads;
+      float x[EPT];
+      penalized<E, PEN>(sh.bitmap, pp, E::lds_s(ts + (uint32_t)j * 16u), e_lo + j * EPT, x);
+      const float xq = pick(x, q);
+      const float sv = t_one ? xq : div_by_const(xq, T, rT);
+      const uint32_t slot = atomicAdd(&rg.nlist, 1u);
+      if (slot < (uint32_t)kCandCap) sh.cand[slot] = rank_key(sv, e_lo + j * EPT + q);
     }
   }
 }
@@ -535,7 +540,7 @@ __device__ __noinline__ int stream_topk(Ring* rgp, unsigned char* ring, Pen pp, 
   RowAcc acc{-INFINITY, -INFINITY, INT_MAX, 0.0};
   for (int c = 0; c < g.nchunk; ++c, ++n) {
     const ChunkPos p = chunk_at(rg, ring, g, n, c > 0, status);
-    if (c == 0 || c == kRefreshChunk) {
+    if (c == 0 || (c == kRefreshChunk && k > kRefreshMinK)) {
       // the maxima first, then the (new) bound, then the candidates
       max_pass<E, PEN>(p.tile, sh.bitmap, pp, p.e_lo, p.nsl, tid, acc);
       topk_bound8(&rg, acc.st, k, t_one, T, rT, tid);
@@ -596,26 +601,29 @@ __device__ __forceinline__ int stream_mass_sel(bool t_one, bool hist, Ring* rgp,
 }
 
 // ---------------------------------------------------------------- the second pass
-// A top-p row's second pass through the ring (pieces of 32 consecutive
-// 16-byte slots: one warp's round over a chunk).  With `collect`: the exact
-// mass above the window [wlo, whi] in a fixed summation order (returned), the
-// kept mass of every piece (pm2[chunk * ppc + piece], fp32, in vocabulary
-// order) and, with `take_members`, the window's members appended to sh.cand
-// (ctl.cand_n); otherwise the chunks are only released.  The work on a batch
-// of slots is straight-line (a bit mask flags the rare window members), so the
-// block's few warps keep many independent instructions in flight; the row's
-// constants come by value and stay in registers.  Consumer threads.
+// A top-p row's second pass through the ring.  Its pieces are kPieceSlots
+// consecutive 16-byte slots of a chunk: warp w reads piece w of every chunk,
+// slots kPieceSlots * w + 32 r + lane for its kRounds rounds.  With
+// `collect`: the exact mass above the window [wlo, whi] in a fixed summation
+// order (returned), the kept mass of every piece (pm2[chunk * ppc + piece],
+// fp32, in vocabulary order) and, with `take_members`, the window's members
+// appended to sh.cand (ctl.cand_n); otherwise the chunks are only released.
+// The work on a piece is straight-line: a bit mask flags the rare window
+// members, which a short loop then re-reads from the ring and appends, and
+// one warp reduction per chunk gives the piece's mass.  The row's constants
+// come by value and stay in registers.  Consumer threads.
 template <class E, bool PEN, bool TONE>
 __device__ __noinline__ double ring_pass2(Ring* rgp, Pen pp, float T, float rT, float m0, uint32_t wlo, uint32_t whi,
                                           bool take_members, float* pm2, int ppc, bool collect, int tid) {
   constexpr int EPT = E::kEPT;
+  static_assert(kRounds * EPT <= 32, "one member bit per element of a piece");
   Ring& rg = *rgp;
   const Geo g = rg.geo;
   const Sh sh = rg.sh;
   Ctl& ctl = *sh.ctl;
   uint32_t* const status = rg.args.status;
   unsigned char* ring = reinterpret_cast<unsigned char*>(rgp) + g.o_ring;
-  const int lane = tid & 31;
+  const int lane = tid & 31, warp = tid >> 5;
   const uint32_t span = whi - wlo;
   int n = rg.n;
   double la = 0.0;
@@ -624,64 +632,61 @@ __device__ __noinline__ double ring_pass2(Ring* rgp, Pen pp, float T, float rT, 
     if (tid == 0) ctl.cand_n = 0u;
     csync();
   }
+  const int jw = kPieceSlots * warp + lane;  // this thread's first slot of its piece
   for (int c = 0; c < g.nchunk; ++c, ++n) {
     const ChunkPos p = chunk_at(rg, ring, g, n, true, status);
-    if (collect) {
-      const int jend = (p.nsl + kRounds * kThreads - 1) / (kRounds * kThreads) * (kRounds * kThreads);
-      for (int j0 = tid; j0 < jend; j0 += kRounds * kThreads) {
-        Batch<E> b;
-        load_batch_ninf<E>(p.tile, j0, p.nsl, b);
-        // straight-line work on the batch: masses, the mass above the window
-        // per round, and a mask of the window's members (rare)
-        float ps[kRounds];
-        uint32_t memb = 0u;
+    if (collect && kPieceSlots * warp < p.nsl) {  // (warp-uniform)
+      const uint32_t tile = smem_addr(p.tile);
+      typename E::Raw raw[kRounds];
 #pragma unroll
-        for (int r = 0; r < kRounds; ++r) {
-          const int j = j0 + r * kThreads;
-          float x[EPT];
-          const bool live = j < p.nsl;
-          penalized<E, PEN>(sh.bitmap, pp, b.raw[r], p.e_lo + j * EPT, x, live);
-          float part = 0.0f;
-#pragma unroll
-          for (int q = 0; q < EPT; ++q) {
-            const float sv = TONE ? x[q] : div_by_const(x[q], T, rT);
-            const float e = exp_shifted(sv, m0);
-            const uint32_t bits = __float_as_uint(e);
-            part = __fadd_rn(part, bits > whi ? e : 0.0f);  // (+0 leaves the sum as it is)
-            // a window that reaches e = 0 takes -inf logits too, never a slot past the chunk
-            memb |= (take_members && live && bits - wlo <= span) ? (1u << (r * EPT + q)) : 0u;
-          }
-          ps[r] = part;
-          la += (double)part;
-        }
-        if (memb) {
-          // append this thread's window members
-          while (memb) {
-            const int bit = __ffs(memb) - 1;
-            memb &= memb - 1u;
-            const int r = bit / EPT, q = bit % EPT;
-            const int j = j0 + r * kThreads;
-            float x[EPT];
-            penalized<E, PEN>(sh.bitmap, pp, b.raw[r], p.e_lo + j * EPT, x);
-            const float sv = TONE ? x[q] : div_by_const(x[q], T, rT);
-            const uint32_t slot = atomicAdd(&ctl.cand_n, 1u);
-            if (slot < (uint32_t)kCandCap) sh.cand[slot] = rank_key(sv, p.e_lo + j * EPT + q);
-          }
-        }
-        // the rounds' piece masses (32 slots each), summed in a fixed order
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-#pragma unroll
-          for (int r = 0; r < kRounds; ++r) ps[r] += __shfl_xor_sync(0xffffffffu, ps[r], o);
-        }
-        if (lane == 0) {
-#pragma unroll
-          for (int r = 0; r < kRounds; ++r) {
-            const int jr = j0 + r * kThreads;  // this lane's slot: the piece's first
-            if (jr < p.nsl) pm2[c * ppc + (jr >> 5)] = ps[r];
-          }
+      for (int r = 0; r < kRounds; ++r) {
+        const int j = jw + 32 * r;
+        if (j < p.nsl) {
+          raw[r] = E::lds_s(tile + (uint32_t)j * 16u);
+        } else {
+          // past the chunk: -inf logits (no mass, never a member)
+          const uint4 ninf = make_uint4(E::kNegInf2, E::kNegInf2, E::kNegInf2, E::kNegInf2);
+          raw[r] = *reinterpret_cast<const typename E::Raw*>(&ninf);
         }
       }
+      float piece = 0.0f;
+      uint32_t memb = 0u;
+#pragma unroll
+      for (int r = 0; r < kRounds; ++r) {
+        const int j = jw + 32 * r;
+        const bool live = j < p.nsl;
+        float x[EPT];
+        penalized<E, PEN>(sh.bitmap, pp, raw[r], p.e_lo + j * EPT, x, live);
+        float part = 0.0f;
+#pragma unroll
+        for (int q = 0; q < EPT; ++q) {
+          const float sv = TONE ? x[q] : div_by_const(x[q], T, rT);
+          const float e = exp_shifted(sv, m0);
+          const uint32_t bits = __float_as_uint(e);
+          part = __fadd_rn(part, bits > whi ? e : 0.0f);  // (+0 leaves the sum as it is)
+          // a window that reaches e = 0 would take -inf logits too, never a slot past the chunk
+          memb |= (take_members && live && bits - wlo <= span) ? (1u << (r * EPT + q)) : 0u;
+        }
+        la += (double)part;
+        piece = __fadd_rn(piece, part);
+      }
+      while (memb) {
+        // a window member: re-read its slot, append its rank key
+        const int bit = __ffs(memb) - 1;
+        memb &= memb - 1u;
+        const int r = bit / EPT, q = bit % EPT;
+        const int j = jw + 32 * r;
+        float x[EPT];
+        penalized<E, PEN>(sh.bitmap, pp, E::lds_s(tile + (uint32_t)j * 16u), p.e_lo + j * EPT, x);
+        const float xq = pick(x, q);
+        const float sv = TONE ? xq : div_by_const(xq, T, rT);
+        const uint32_t slot = atomicAdd(&ctl.cand_n, 1u);
+        if (slot < (uint32_t)kCandCap) sh.cand[slot] = rank_key(sv, p.e_lo + j * EPT + q);
+      }
+      // the piece's mass, summed in a fixed order
+#pragma unroll
+      for (int o = 16; o; o >>= 1) piece += __shfl_xor_sync(0xffffffffu, piece, o);
+      if (lane == 0) pm2[c * ppc + warp] = piece;
     }
     chunk_done(rg, p.s, false, tid);
   }
@@ -706,7 +711,7 @@ __device__ __forceinline__ int piece_of(const Geo& g, int ppc, int ept, int idx)
   int c = (int)(((idx >> 5) * (int64_t)g.nchunk) / g.units);
   while (c + 1 < g.nchunk && chunk_lo(g, c + 1) <= idx) ++c;
   while (c > 0 && chunk_lo(g, c) > idx) --c;
-  return c * ppc + (((idx - chunk_lo(g, c)) / ept) >> 5);
+  return c * ppc + ((idx - chunk_lo(g, c)) / ept) / kPieceSlots;
 }
 
 // Adds the kept window members (rank key <= last) to their pieces' masses.
@@ -724,7 +729,7 @@ __device__ void members_to_pieces(const Geo& g, const Sh& sh, int nmem, unsigned
 
 // Inverse-CDF draw in vocabulary order over the piece masses of the second
 // pass: a block scan finds the piece whose mass prefix passes `target`, then
-// warp 0 reads that piece (one round trip) and walks it.  Falls back to the
+// warp 0 reads that piece (one round trip for its kRounds rounds) and walks it.  Falls back to the
 // last kept element when rounding leaves the target past the total, then to
 // `fallback`.  Consumer threads; every thread returns the token.
 template <class E>
@@ -779,44 +784,55 @@ __device__ int draw_ring(Ring& rg, const Sh& sh, const RowCtx& R, const Keep& K,
   }
   if (pc < 0) return fallback;
   if (warp == 0) {
+    // the piece's rounds in vocabulary order: slots kPieceSlots * w + 32 r + lane
     const int c = pc / ppc, w = pc % ppc;
     const int e_lo = chunk_lo(g, c), e_hi = min(R.V, chunk_lo(g, c + 1));
-    const int slot = 32 * w + lane;
-    const int idx0 = e_lo + slot * EPT;
-    const bool valid = idx0 < e_hi;
-    const typename E::Raw raw = valid ? E::ldg(R.src + (size_t)idx0 * esz) : E::zero();
-    float q[EPT];
-    kept_masses<E>(R, sh.bitmap, K, raw, idx0, valid, q);
-    float ls = 0.f;
-    int lk = -1;
+    typename E::Raw raw[kRounds];
 #pragma unroll
-    for (int j = 0; j < EPT; ++j) {
-      ls = __fadd_rn(ls, q[j]);
-      if (q[j] > 0.f) lk = idx0 + j;
+    for (int r = 0; r < kRounds; ++r) {
+      const int idx0 = e_lo + (kPieceSlots * w + 32 * r + lane) * EPT;
+      raw[r] = idx0 < e_hi ? E::ldg(R.src + (size_t)idx0 * esz) : E::zero();
     }
-    const int lastk = (int)__reduce_max_sync(0xffffffffu, (uint32_t)(lk + 1)) - 1;
-    const double inc2 = warp_incl_f64((double)ls, lane);
-    const uint32_t bal = __ballot_sync(0xffffffffu, inc2 > t2 && ls > 0.f);
-    int tok = lastk >= 0 ? lastk : fallback;
-    if (bal) {
-      const int l = __ffs(bal) - 1;
-      int mine = -1;
-      if (lane == l) {
-        double cum = inc2 - (double)ls;
-        int pk = -1, lastc = -1;
+    int tok = -1, lastk = -1;
+    double run2 = 0.0;  // kept mass of the piece's earlier rounds
 #pragma unroll
-        for (int j = 0; j < EPT; ++j) {
-          if (q[j] > 0.f) {
-            lastc = j;
-            cum += (double)q[j];
-            if (pk < 0 && cum > t2) pk = j;
-          }
-        }
-        if (pk < 0) pk = lastc;
-        mine = idx0 + pk;
+    for (int r = 0; r < kRounds; ++r) {
+      if (tok >= 0) break;  // (warp-uniform)
+      const int idx0 = e_lo + (kPieceSlots * w + 32 * r + lane) * EPT;
+      float q[EPT];
+      kept_masses<E>(R, sh.bitmap, K, raw[r], idx0, idx0 < e_hi, q);
+      float ls = 0.f;
+      int lk = -1;
+#pragma unroll
+      for (int j = 0; j < EPT; ++j) {
+        ls = __fadd_rn(ls, q[j]);
+        if (q[j] > 0.f) lk = idx0 + j;
       }
-      tok = __shfl_sync(0xffffffffu, mine, l);
+      lastk = max(lastk, (int)__reduce_max_sync(0xffffffffu, (uint32_t)(lk + 1)) - 1);
+      const double inc2 = warp_incl_f64((double)ls, lane) + run2;
+      const uint32_t bal = __ballot_sync(0xffffffffu, inc2 > t2 && ls > 0.f);
+      if (bal) {
+        const int l = __ffs(bal) - 1;
+        int mine = -1;
+        if (lane == l) {
+          double cum = inc2 - (double)ls;
+          int pk = -1, lastc = -1;
+#pragma unroll
+          for (int j = 0; j < EPT; ++j) {
+            if (q[j] > 0.f) {
+              lastc = j;
+              cum += (double)q[j];
+              if (pk < 0 && cum > t2) pk = j;
+            }
+          }
+          if (pk < 0) pk = lastc;
+          mine = idx0 + pk;
+        }
+        tok = __shfl_sync(0xffffffffu, mine, l);
+      }
+      run2 = __shfl_sync(0xffffffffu, inc2, 31);
     }
+    if (tok < 0) tok = lastk >= 0 ? lastk : fallback;
     if (lane == 0) ctl.token = tok;
   }
   csync();
@@ -1564,8 +1580,8 @@ static int rows_launch_ws(const NsSampleArgs& a, cudaStream_t stream, int device
   nchunk = nchunk < 1 ? 1 : (nchunk > kMaxChunksRow ? kMaxChunksRow : nchunk);
   g.nchunk = nchunk;
   g.slot_bytes = ((g.units + nchunk - 1) / nchunk) * kUnit * esz;
-  g.ppc = (g.slot_bytes + 511) / 512;
-  if (g.nchunk * g.ppc > kPm2Cap) {
+  g.ppc = (g.slot_bytes + 16 * kPieceSlots - 1) / (16 * kPieceSlots);  // at most kWarps: slots <= 32 KB
+  if (g.ppc > kWarps || g.nchunk * g.ppc > kPm2Cap) {
     err = "ns_sample: too many second-pass pieces per row";
     return NS_ERR_UNSUPPORTED;
   }
