@@ -338,7 +338,7 @@ def test_config3_bf16_gather_without_debug_outputs():
 @pytest.mark.parametrize("V", [32768, 128256])
 def test_top_k_rows_without_debug_outputs(V, dtype):
     """Top-k rows as served (no debug outputs), mixed with top-p rows that take
-    the pre-pass: ties at the k-th value, k = 1, k = 128 and k = 129 (past the
+    the second ring pass: ties at the k-th value, k = 1, k = 128 and k = 129 (past the
     candidate-list path), top-k with top-p, the penalty, NaN / +inf / all -inf
     rows, a flat row and a mostly -inf row (candidate lists that overflow into
     the general path) all give the oracle's tokens."""
