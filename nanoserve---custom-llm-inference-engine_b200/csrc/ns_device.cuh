@@ -194,10 +194,26 @@ __device__ __forceinline__ float div_by_const(float x, float t, float r) {
 __device__ __forceinline__ float penalize(float x, float rp) {
   return (x < 0.0f) ? __fmul_rn(x, rp) : div_rn_out_of_line(x, rp);
 }
-// The same with rrp = RN(1/rp): the division by the row constant rp goes
-// through div_by_const (bit-exact, IEEE division only at extreme operands).
-__device__ __forceinline__ float penalize(float x, float rp, float rrp) {
-  return (x < 0.0f) ? __fmul_rn(x, rp) : div_by_const(x, rp, rrp);
+// x / rp rounded to fp32 as IEEE division rounds it, for every x and rp,
+// with no branch and no call (so that it can sit in unrolled streaming loops):
+// given inv = RN64(1/rp), q0 = RN64(x inv) and one FMA correction give q1
+// within an fp64 ulp of x / rp.  A quotient of two 24-bit significands is
+// never that close to a midpoint of two fp32 neighbours (nor exactly on one),
+// so RN32(q1) = RN32(x / rp); fp64 holds every such quotient without overflow
+// or underflow.  When q0 is zero, infinite or NaN (x = 0, x = +-inf or NaN,
+// rp = 0, +-inf or NaN) the correction would turn it into NaN, and q0 itself
+// is already the IEEE result.
+__device__ __forceinline__ float div_by_row_const(float x, float rp, double inv) {
+  const double xd = (double)x;
+  const double q0 = xd * inv;
+  const double q1 = fma(fma(-q0, (double)rp, xd), inv, q0);
+  return (float)((q0 != 0.0 && fabs(q0) <= 1.7976931348623157e308) ? q1 : q0);
+}
+
+// The same with inv = RN64(1/rp) (the row's constant): no out-of-line
+// division path.
+__device__ __forceinline__ float penalize(float x, float rp, double inv) {
+  return (x < 0.0f) ? __fmul_rn(x, rp) : div_by_row_const(x, rp, inv);
 }
 
 // Approximate mass of one positive normal float for the top-p locator

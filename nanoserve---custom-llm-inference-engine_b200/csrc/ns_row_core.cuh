@@ -163,7 +163,9 @@ struct Sh {
 // One row being sampled, with the row layout shared by every row.
 // Repetition penalty of a row: rp and RN(1/rp).
 struct Pen {
-  float rp, rrp;
+  float rp;
+  double inv;  // RN64(1 / rp)
+  __device__ static Pen of(float rp) { return Pen{rp, __drcp_rn((double)rp)}; }
 };
 
 struct RowCtx {
@@ -239,7 +241,7 @@ __device__ __forceinline__ void penalized(const uint32_t* bitmap, Pen pp, const 
     if (m) {
 #pragma unroll
       for (int j = 0; j < E::kEPT; ++j)
-        if ((m >> j) & 1u) x[j] = penalize(x[j], pp.rp, pp.rrp);
+        if ((m >> j) & 1u) x[j] = penalize(x[j], pp.rp, pp.inv);
     }
   }
 }

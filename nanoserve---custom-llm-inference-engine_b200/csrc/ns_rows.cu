@@ -876,7 +876,7 @@ __device__ __noinline__ void finish_row(Ring* rgp, int tid) {
   R.p = P.top_p;
   R.k = (P.top_k > 0 && P.top_k < V) ? P.top_k : 0;
   R.rp = P.repetition_penalty;
-  R.pp = Pen{R.rp, __frcp_rn(R.rp)};
+  R.pp = Pen::of(R.rp);
   R.pen = (P.flags & NS_ROW_PENALTY) != 0u && a.history_offsets && d.h1 > d.h0;
   int mode = row_mode(P, V, debug);
   const bool hist_used = (mode == kGeneral) && R.k == 0 && R.topp;  // the chunks built sh.hist
@@ -1452,7 +1452,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) rows_kernel(const NsSampleAr
       const float rT = __frcp_rn(T);
       const bool t_one = (T == 1.0f);
       const bool pen = (P.flags & NS_ROW_PENALTY) != 0u && a.history_offsets && h1 > h0;
-      const Pen pp{P.repetition_penalty, __frcp_rn(P.repetition_penalty)};
+      const Pen pp = Pen::of(P.repetition_penalty);
       const bool with_e = (mode == kGeneral) && k == 0;
       const bool want_hist = with_e && (P.flags & NS_ROW_TOP_P) != 0u;
 
