@@ -332,7 +332,7 @@ __device__ __forceinline__ void max_pass(const unsigned char* tile, const uint32
 // maximum bookkeeping rides along.
 template <class E, bool PEN, bool TONE, bool HIST, bool TRACK>
 __device__ __forceinline__ void mass_pass(const unsigned char* tile, const uint32_t* bitmap, uint32_t* hist, Pen pp,
-                                          float T, float rT, float m0, int e_lo, int nsl, int tid, RowAcc& acc) {
+                                          float T, double invT, float m0, int e_lo, int nsl, int tid, RowAcc& acc) {
   const uint32_t hs = smem_addr(hist);
   for (int j0 = tid; j0 < nsl; j0 += kRounds * kThreads) {
     Batch<E> b;
@@ -347,7 +347,7 @@ __device__ __forceinline__ void mass_pass(const unsigned char* tile, const uint3
         float part = 0.0f;
 #pragma unroll
         for (int q = 0; q < E::kEPT; ++q) {
-          const float sv = TONE ? x[q] : div_by_const(x[q], T, rT);
+          const float sv = TONE ? x[q] : div_by_row_const(x[q], T, invT);
           const float e = exp_shifted(sv, m0);
           part = __fadd_rn(part, e);
           if (HIST) {
@@ -370,7 +370,7 @@ __device__ __forceinline__ void mass_pass(const unsigned char* tile, const uint3
 // from the ring.
 template <class E, bool PEN, bool TRACK>
 __device__ __forceinline__ void cand_pass(const unsigned char* tile, const Sh& sh, Ring& rg, Pen pp, float tau,
-                                          bool t_one, float T, float rT, int e_lo, int nsl, int tid, RowAcc& acc) {
+                                          bool t_one, float T, double invT, int e_lo, int nsl, int tid, RowAcc& acc) {
   constexpr int EPT = E::kEPT;
   static_assert(kRounds * EPT <= 32, "one candidate bit per element of a batch");
   const uint32_t ts = smem_addr(tile);
@@ -396,7 +396,7 @@ __device__ __forceinline__ void cand_pass(const unsigned char* tile, const Sh& s
       float x[EPT];
       penalized<E, PEN>(sh.bitmap, pp, E::lds_s(ts + (uint32_t)j * 16u), e_lo + j * EPT, x);
       const float xq = pick(x, q);
-      const float sv = t_one ? xq : div_by_const(xq, T, rT);
+      const float sv = t_one ? xq : div_by_row_const(xq, T, invT);
       const uint32_t slot = atomicAdd(&rg.nlist, 1u);
       if (slot < (uint32_t)kCandCap) sh.cand[slot] = rank_key(sv, e_lo + j * EPT + q);
     }
@@ -537,6 +537,7 @@ __device__ __noinline__ int stream_topk(Ring* rgp, unsigned char* ring, Pen pp, 
   Ring& rg = *rgp;
   const Geo g = rg.geo;
   const Sh sh = rg.sh;
+  const double invT = t_one ? 1.0 : __drcp_rn((double)T);  // (the quotients stay IEEE; no call in the loops)
   RowAcc acc{-INFINITY, -INFINITY, INT_MAX, 0.0};
   for (int c = 0; c < g.nchunk; ++c, ++n) {
     const ChunkPos p = chunk_at(rg, ring, g, n, c > 0, status);
@@ -544,9 +545,9 @@ __device__ __noinline__ int stream_topk(Ring* rgp, unsigned char* ring, Pen pp, 
       // the maxima first, then the (new) bound, then the candidates
       max_pass<E, PEN>(p.tile, sh.bitmap, pp, p.e_lo, p.nsl, tid, acc);
       topk_bound8(&rg, acc.st, k, t_one, T, rT, tid);
-      cand_pass<E, PEN, false>(p.tile, sh, rg, pp, rg.bound, t_one, T, rT, p.e_lo, p.nsl, tid, acc);
+      cand_pass<E, PEN, false>(p.tile, sh, rg, pp, rg.bound, t_one, T, invT, p.e_lo, p.nsl, tid, acc);
     } else {
-      cand_pass<E, PEN, true>(p.tile, sh, rg, pp, rg.bound, t_one, T, rT, p.e_lo, p.nsl, tid, acc);
+      cand_pass<E, PEN, true>(p.tile, sh, rg, pp, rg.bound, t_one, T, invT, p.e_lo, p.nsl, tid, acc);
     }
     chunk_done(rg, p.s, c == g.nchunk - 1, tid);
   }
@@ -561,6 +562,7 @@ __device__ __noinline__ int stream_mass(Ring* rgp, unsigned char* ring, Pen pp, 
   const Geo g = rg.geo;
   const Sh sh = rg.sh;
   const int lane = tid & 31;
+  const double invT = TONE ? 1.0 : __drcp_rn((double)T);  // (the quotients stay IEEE; no call in the loops)
   RowAcc acc{-INFINITY, -INFINITY, INT_MAX, 0.0};
   // chunk 0: its maximum gives m0, then its masses
   {
@@ -575,14 +577,14 @@ __device__ __noinline__ int stream_mass(Ring* rgp, unsigned char* ring, Pen pp, 
     const float m0 = (mx > -INFINITY && mx < INFINITY) ? (TONE ? mx : div_by_const(mx, T, rT)) : 0.0f;
     if (tid == 0) rg.m0 = m0;
     csync();  // rg.wkey is reused
-    mass_pass<E, PEN, TONE, HIST, false>(p.tile, sh.bitmap, sh.hist, pp, T, rT, m0, p.e_lo, p.nsl, tid, acc);
+    mass_pass<E, PEN, TONE, HIST, false>(p.tile, sh.bitmap, sh.hist, pp, T, invT, m0, p.e_lo, p.nsl, tid, acc);
     chunk_done(rg, p.s, g.nchunk == 1, tid);
     ++n;
   }
   const float m0 = rg.m0;
   for (int c = 1; c < g.nchunk; ++c, ++n) {
     const ChunkPos p = chunk_at(rg, ring, g, n, true, status);
-    mass_pass<E, PEN, TONE, HIST, true>(p.tile, sh.bitmap, sh.hist, pp, T, rT, m0, p.e_lo, p.nsl, tid, acc);
+    mass_pass<E, PEN, TONE, HIST, true>(p.tile, sh.bitmap, sh.hist, pp, T, invT, m0, p.e_lo, p.nsl, tid, acc);
     chunk_done(rg, p.s, c == g.nchunk - 1, tid);
   }
   *out = acc;
@@ -625,6 +627,8 @@ __device__ __noinline__ double ring_pass2(Ring* rgp, Pen pp, float T, float rT, 
   unsigned char* ring = reinterpret_cast<unsigned char*>(rgp) + g.o_ring;
   const int lane = tid & 31, warp = tid >> 5;
   const uint32_t span = whi - wlo;
+  const double invT = TONE ? 1.0 : __drcp_rn((double)T);  // (T / rT: the IEEE quotient, no call in the loop)
+  (void)rT;
   int n = rg.n;
   double la = 0.0;
   if (collect) {
@@ -660,7 +664,7 @@ __device__ __noinline__ double ring_pass2(Ring* rgp, Pen pp, float T, float rT, 
         float part = 0.0f;
 #pragma unroll
         for (int q = 0; q < EPT; ++q) {
-          const float sv = TONE ? x[q] : div_by_const(x[q], T, rT);
+          const float sv = TONE ? x[q] : div_by_row_const(x[q], T, invT);
           const float e = exp_shifted(sv, m0);
           const uint32_t bits = __float_as_uint(e);
           part = __fadd_rn(part, bits > whi ? e : 0.0f);  // (+0 leaves the sum as it is)
@@ -679,7 +683,7 @@ __device__ __noinline__ double ring_pass2(Ring* rgp, Pen pp, float T, float rT, 
         float x[EPT];
         penalized<E, PEN>(sh.bitmap, pp, E::lds_s(tile + (uint32_t)j * 16u), p.e_lo + j * EPT, x);
         const float xq = pick(x, q);
-        const float sv = TONE ? xq : div_by_const(xq, T, rT);
+        const float sv = TONE ? xq : div_by_row_const(xq, T, invT);
         const uint32_t slot = atomicAdd(&ctl.cand_n, 1u);
         if (slot < (uint32_t)kCandCap) sh.cand[slot] = rank_key(sv, p.e_lo + j * EPT + q);
       }
