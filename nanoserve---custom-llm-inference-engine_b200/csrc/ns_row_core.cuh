@@ -172,6 +172,7 @@ struct RowCtx {
   const char* src;
   int V, W, nch, row;
   float T, rT, rp, p;
+  double invT;  // RN64(1 / T): scaled() divides with no out-of-line call
   Pen pp;
   int k;  // top-k (0: none)
   bool t_one, greedy, topp, pen;
@@ -215,7 +216,7 @@ __device__ __forceinline__ int row_mode(const NsRowParams& P, int V, bool debug)
 }
 
 __device__ __forceinline__ float scaled(const RowCtx& R, float x) {
-  return R.t_one ? x : div_by_const(x, R.T, R.rT);
+  return R.t_one ? x : div_by_row_const(x, R.T, R.invT);
 }
 
 // Smallest float c <= b with RN(c/T) == RN(b/T): the lower end of the set of

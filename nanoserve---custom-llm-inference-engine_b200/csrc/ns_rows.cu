@@ -875,6 +875,7 @@ __device__ __noinline__ void finish_row(Ring* rgp, int tid) {
   R.greedy = (P.flags & NS_ROW_GREEDY) != 0u;
   R.T = R.greedy ? 1.0f : P.temperature;
   R.rT = __frcp_rn(R.T);
+  R.invT = __drcp_rn((double)R.T);
   R.t_one = (R.T == 1.0f);
   R.topp = (P.flags & NS_ROW_TOP_P) != 0u;
   R.p = P.top_p;
@@ -1230,7 +1231,7 @@ __device__ __noinline__ void finish_row(Ring* rgp, int tid) {
               for (int j = 0; j < EPT; ++j) s[j] = x[j];
             } else {
 #pragma unroll
-              for (int j = 0; j < EPT; ++j) s[j] = div_by_const(x[j], R.T, R.rT);
+              for (int j = 0; j < EPT; ++j) s[j] = div_by_row_const(x[j], R.T, R.invT);
             }
             bool anym = false;
             uint32_t bits[EPT];
