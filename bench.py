@@ -15,7 +15,7 @@ all-gather of the int32 ids (weak scaling), and the max over ranks is taken.
 
 The JSON line also carries:
 
-* ``roofline``: achieved HBM GB/s of the split-row kernel (algorithmic bytes
+* ``roofline``: achieved HBM GB/s of the row kernel (algorithmic bytes
   over its CUDA-event time) against MEASURED_PEAKS.json; ``traffic`` is the
   DRAM bytes per launch of the ncu capture named in ``traffic_source``;
 * ``us_per_step_p50``: the median of per-step times (one-step graph replays,
@@ -101,7 +101,7 @@ def measured_peaks():
 
 
 def profiled_traffic():
-    """DRAM bytes per launch of the split-row kernel in the committed ncu summary."""
+    """DRAM bytes per launch of the row kernel in the committed ncu summary."""
     if not PROFILE.exists():
         return None
     m = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", PROFILE.read_text())
@@ -575,7 +575,7 @@ def run_ours(args):
             "path": ("HistoryStore.sample(logits resident in HBM, histories on the device, row params packed and "
                      "uploaded) + ids .cpu(): the engine-side path"),
         },
-        # one split-row kernel launch per step
+        # one row-kernel launch per step
         "gpu_launches": K,
         "clocks": clocks.summary(),
     }

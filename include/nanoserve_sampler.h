@@ -55,11 +55,12 @@ extern "C" {
 #define NS_OUT_I64 0
 #define NS_OUT_I32 1
 
-/* NsSampleArgs.kernel: which kernel serves the call */
-#define NS_KERNEL_AUTO 0     /* split-row for batches of >= 32 aligned rows,
+/* NsSampleArgs.kernel: which kernel serves the call ("split": the row
+ * kernel, which splits a batch's rows over persistent blocks, one per SM) */
+#define NS_KERNEL_AUTO 0     /* the row kernel for batches of >= 32 aligned rows,
                                 the cluster kernel otherwise              */
 #define NS_KERNEL_CLUSTER 1  /* always the cluster kernel                 */
-#define NS_KERNEL_SPLIT 2    /* the split-row kernel where its layout
+#define NS_KERNEL_SPLIT 2    /* the row kernel where its layout
                                 conditions hold (aligned rows, vocabulary
                                 in [24576, 196608]), else the cluster one */
 

@@ -1,4 +1,4 @@
-// ns_row_core.cuh -- device building blocks of the split-row sampling kernel
+// ns_row_core.cuh -- device building blocks of the row sampling kernel
 // (ns_rows.cu): element formats, the row layout used by its whole-row passes,
 // block reductions and sorts over the 512 consumer threads, the exact top-k
 // radix select, the top-p window search, member decision and tie resolution,

@@ -1,4 +1,4 @@
-// ns_rows.h -- host-side entry points of the split-row sampling kernel
+// ns_rows.h -- host-side entry points of the row sampling kernel
 // (ns_rows.cu), used by ns_sample() in ns_sample.cu.
 #pragma once
 
@@ -10,7 +10,7 @@
 
 namespace ns {
 
-// True when the split-row kernel can serve this call: 16-byte aligned rows
+// True when the row kernel can serve this call: 16-byte aligned rows
 // whose byte length is a multiple of 16 and a vocabulary in the supported
 // range.
 bool rows_supported(const NsSampleArgs& a);
@@ -18,7 +18,7 @@ bool rows_supported(const NsSampleArgs& a);
 // Bytes of workspace for calls of up to num_rows rows (ns_workspace_bytes).
 int64_t rows_workspace_bytes(int32_t num_rows);
 
-// Launches the split-row kernel on a.workspace; returns NS_OK or an NS_ERR_*
+// Launches the row kernel on a.workspace; returns NS_OK or an NS_ERR_*
 // code with `err` set.
 int rows_launch(const NsSampleArgs& a, cudaStream_t stream, int device, std::string& err);
 

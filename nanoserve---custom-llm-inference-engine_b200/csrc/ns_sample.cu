@@ -1832,7 +1832,7 @@ struct DeviceState {
 std::mutex g_mu;
 DeviceState g_dev[64];
 
-// Batches of at least this many rows use the split-row kernel.
+// Batches of at least this many rows use the row kernel.
 constexpr int kRowsMinBatch = 32;
 
 int slice_width(int V) {
@@ -1859,7 +1859,7 @@ int64_t ns_workspace_bytes(int32_t num_rows) { return ns::rows_workspace_bytes(n
 
 namespace ns {
 
-// One sampling step (ns_sample's body).  `noalloc`: the split-row kernel runs
+// One sampling step (ns_sample's body).  `noalloc`: the row kernel runs
 // on the library's static workspace (ns_sample_noalloc).
 static int sample_call(const NsSampleArgs* args, void* stream, bool noalloc) {
   if (!args) return fail(NS_ERR_INVALID_ARG, "ns_sample: args is NULL");
@@ -1897,7 +1897,7 @@ static int sample_call(const NsSampleArgs* args, void* stream, bool noalloc) {
 
   if (a.kernel != NS_KERNEL_AUTO && a.kernel != NS_KERNEL_CLUSTER && a.kernel != NS_KERNEL_SPLIT)
     return fail(NS_ERR_INVALID_ARG, "ns_sample: kernel must be NS_KERNEL_AUTO, NS_KERNEL_CLUSTER or NS_KERNEL_SPLIT");
-  // Kernel choice: the split-row kernel once the batch is large enough, the
+  // Kernel choice: the row kernel once the batch is large enough, the
   // cluster kernel otherwise (NsSampleArgs.kernel may force either).
   if (rows_supported(a) && (a.kernel == NS_KERNEL_SPLIT || (a.kernel == NS_KERNEL_AUTO && a.num_rows >= kRowsMinBatch))) {
     std::string msg;

@@ -100,10 +100,11 @@ def derive_rows(params: Sequence, vocab: int, hist_lens) -> np.ndarray:
     return rows
 
 
-# Relative length of a row's finishing work on the split-row kernel (the
-# block that summarises its last part finishes it): greedy rows only merge
-# numbers, top-k <= 128 rows sort a short candidate list, plain sampling and
-# top-p rows re-read the row, large top-k rows re-read it several times.
+# Relative cost of a row on the row kernel: greedy rows stream once and only
+# track the maximum, top-k <= 128 rows also keep a candidate list and sort it,
+# plain sampling re-reads the row for its draw, top-p rows stream twice (the
+# boundary window is collected on a second pass) and rank the window's
+# members, large top-k rows re-read the row several times.
 TOPK_LIST_MAX = 128
 COST_GREEDY, COST_TOPK, COST_PLAIN, COST_TOPP, COST_LARGE_K = 1, 3, 5, 7, 8
 
@@ -125,12 +126,11 @@ def row_costs(row_params: np.ndarray) -> np.ndarray:
 def schedule(row_params: np.ndarray, sms: int) -> np.ndarray:
     """Row order for ``NsSampleArgs.row_order``: the most expensive rows first.
 
-    The split-row kernel hands out the parts of row position 0 first, then
-    those of position 1, and so on; a row's finishing work runs as soon as its
-    last part is summarised, while later rows stream.  Putting the rows with
-    the longest finishing work first lets that work overlap the streaming of
-    the cheap rows, which end the step.  (``sms`` only says that the caller
-    has a GPU to schedule for; the order does not depend on its size.)
+    The row kernel's persistent blocks claim rows in this order, one at a
+    time, as they finish the previous one (longest-processing-time-first
+    list scheduling): the costly rows start at once and the cheap rows fill
+    the gaps at the end of the step.  (``sms`` only says that the caller has
+    a GPU to schedule for; the order does not depend on its size.)
     """
     S = row_params.shape[0]
     if S == 0 or sms <= 0:

@@ -132,7 +132,8 @@ KERNELS = {"auto": 0, "cluster": 1, "split": 2}
 class Sampler:
     """B200 sampling op with the reference ``Sampler`` interface.
 
-    ``kernel`` picks the CUDA kernel: ``"auto"`` (the split-row kernel for
+    ``kernel`` picks the CUDA kernel: ``"auto"`` (the row kernel, whose
+    persistent blocks split the batch's rows among the SMs, for
     batches of at least 32 aligned rows, the cluster kernel otherwise),
     ``"cluster"`` or ``"split"`` (where its layout conditions hold)."""
 

@@ -64,7 +64,7 @@ def _full_size(config: int):
 @pytest.mark.parametrize("config", [4, 5])
 def test_full_size_batches(config, debug):
     """More than twice as many rows as the GPU has SMs in one call, so every
-    persistent block of either kernel takes many rows (and the split-row
+    persistent block of either kernel takes many rows (and the row
     kernel reuses its workspace slots): bit-exact penalised and filtered
     logits, |dp| <= 1e-6 and the oracle's tokens (debug on), the oracle's
     tokens (debug off)."""
